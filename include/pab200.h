@@ -1,0 +1,198 @@
+/*
+ * pab200.h — C ABI of the B200 (sm_100a) paged-attention decode library
+ * (libpab200.so).
+ *
+ * The reference (lashhw/pagedattention) is a Python package whose paged
+ * decode path is a Python wrapper over two Triton kernels:
+ *   flash_attn_with_kvcache_wrapper_triton   src/kernel_triton.py:181-307
+ *     ├─ host chunk planner                  src/kernel_triton.py:206-243
+ *     ├─ _paged_attention_decode_split_kernel src/kernel_triton.py:8-117
+ *     └─ _paged_attention_decode_reduce_kernel src/kernel_triton.py:120-174
+ * with the eager PyTorch path (src/kernel_eager.py:29-56) as its numerics
+ * reference and the argument contract in src/common.py:1-29.  This header is
+ * the native boundary that replaces that wrapper: plain device pointers,
+ * element strides and sizes, no framework types.  The Python mirror of the
+ * reference interface (pagedattention_b200/kernel_b200.py) binds it with
+ * ctypes.
+ *
+ * Conventions
+ *  - Every pointer in pab200_decode_args is a DEVICE pointer on the current
+ *    CUDA device.  Strides are in ELEMENTS, not bytes.
+ *  - Calls are asynchronous on `stream`; the library never synchronises the
+ *    device, never allocates device memory and keeps no per-call state
+ *    outside the caller's workspace.  Two calls that overlap in time on the
+ *    GPU must not share a workspace.
+ *  - Return value: PAB200_OK (0) or a negative pab200_status code; the text of
+ *    the last error on the calling thread is available from
+ *    pab200_last_error().
+ */
+#ifndef PAB200_H_
+#define PAB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PAB200_ABI_VERSION 1
+
+/* Status codes. */
+typedef enum pab200_status {
+  PAB200_OK = 0,
+  PAB200_ERR_INVALID_ARGUMENT = -1, /* bad shape, size or null pointer       */
+  PAB200_ERR_UNSUPPORTED = -2,      /* valid but not built: dtype, D, bs, G  */
+  PAB200_ERR_WORKSPACE = -3,        /* workspace missing or too small        */
+  PAB200_ERR_ALIGNMENT = -4,        /* pointer or stride alignment           */
+  PAB200_ERR_CUDA = -5              /* CUDA runtime / driver error           */
+} pab200_status;
+
+/* Element type of q, k_cache, v_cache and out. */
+typedef enum pab200_dtype {
+  PAB200_DTYPE_BF16 = 0,
+  PAB200_DTYPE_F16 = 1,
+  PAB200_DTYPE_F32 = 2 /* only as the output type of pab200_merge_states */
+} pab200_dtype;
+
+/* Physical layout of k_cache / v_cache.
+ *  PAB200_LAYOUT_PAGES: [num_pages, block_size, head_size]; one page holds one
+ *    (sequence, kv head)'s block of tokens — the reference layout,
+ *    src/common.py:6-7.  A vLLM-style [num_blocks, num_kv_heads, block_size,
+ *    head_size] ("HND") pool is the same memory seen as num_blocks*num_kv_heads
+ *    pages, addressed with bt_page_mul = num_kv_heads, bt_page_add = 1.
+ *  PAB200_LAYOUT_NHD: [num_pages, block_size, num_kv_heads, head_size]; one
+ *    page holds a block of tokens for all kv heads (the layout the reference's
+ *    vLLM adapter hands to flash-attn, src/kernel_vllm.py:17-26). */
+typedef enum pab200_layout {
+  PAB200_LAYOUT_PAGES = 0,
+  PAB200_LAYOUT_NHD = 1
+} pab200_layout;
+
+/* Device-side error bits, accumulated in the workspace status word and read
+ * with pab200_read_status(). */
+#define PAB200_STATUS_BAD_PAGE_ID 0x1u   /* page id outside [0, num_pages)    */
+#define PAB200_STATUS_SEQLEN_CLAMP 0x2u  /* seqlen > max_blocks*block_size    */
+#define PAB200_STATUS_NEG_SEQLEN 0x4u    /* seqlen < 0 (treated as 0)         */
+#define PAB200_STATUS_WAIT_TIMEOUT 0x8u  /* a pipeline wait hit its time limit */
+
+/* Arguments of one batched paged decode call.
+ *
+ * For sequence s in [0, num_seqs), kv head h in [0, num_kv_heads) and query
+ * head g in [0, G), G = num_q_heads / num_kv_heads, the call computes
+ *   out[s, h*G+g, :] = softmax(q[s, h*G+g, :] . K_{s,h}^T * softmax_scale) V_{s,h}
+ * where K_{s,h}, V_{s,h} are the first L = seqlens(s,h) tokens of the pages
+ *   page(s,h,i) = block_table[s*bt_stride_b + h*bt_stride_h + i*bt_stride_i]
+ *                 * bt_page_mul + h * bt_page_add,      i < ceil(L/block_size)
+ *   seqlens(s,h) = seqlens[s*seqlens_stride_b + h*seqlens_stride_h].
+ * A sequence with L == 0 yields zeros.  This is the contract of
+ * src/common.py:1-14 (with the reference's batch==1 restriction lifted: its
+ * flattened [1, B*Hkv] form is the same call with num_seqs = 1). */
+typedef struct pab200_decode_args {
+  void* out;                 /* [num_seqs, num_q_heads, head_size], dtype    */
+  const void* q;             /* [num_seqs, num_q_heads, head_size], dtype    */
+  const void* k_cache;       /* see pab200_layout; contiguous                */
+  const void* v_cache;       /* same shape as k_cache                        */
+  const int32_t* seqlens;    /* cache_seqlens / context_lens                 */
+  const int32_t* block_table;
+
+  int32_t dtype;             /* pab200_dtype (BF16 or F16)                   */
+  int32_t layout;            /* pab200_layout                                */
+  int32_t num_seqs;          /* B                                            */
+  int32_t num_q_heads;       /* Hq                                           */
+  int32_t num_kv_heads;      /* Hkv                                          */
+  int32_t head_size;         /* D: 64, 128 or 256                            */
+  int32_t block_size;        /* tokens per page: 8, 16, 32 or 64             */
+  int32_t max_blocks;        /* block-table entries per (seq, kv head)       */
+  int64_t num_pages;         /* leading extent of k_cache / v_cache          */
+
+  int64_t q_stride_b, q_stride_h;       /* head_size stride must be 1  */
+  int64_t out_stride_b, out_stride_h;   /* head_size stride must be 1  */
+  int64_t seqlens_stride_b, seqlens_stride_h;  /* h stride 0 => per-seq len */
+  int64_t bt_stride_b, bt_stride_h, bt_stride_i;
+  int32_t bt_page_mul, bt_page_add;
+
+  float softmax_scale;
+  /* Reference meaning (src/kernel_triton.py:206-209): target number of KV
+   * chunks per kv head.  0 or 1: the library sizes the split to the device
+   * (balanced token ranges over every resident warp).  n > 1: at most
+   * num_seqs*num_kv_heads*n ranges. */
+  int32_t num_splits;
+
+  /* Optional cross-device mode.  When state_o is non-null the call writes,
+   * instead of `out`, the normalised fp32 output state_o[s, h*G+g, :]
+   * ([num_seqs, num_q_heads, head_size], contiguous) and its log-sum-exp
+   * state_lse[s, h*G+g] (natural log of sum_t exp(score_t)); an empty range
+   * gives o = 0, lse = -inf.  pab200_merge_states() combines such states. */
+  float* state_o;
+  float* state_lse;
+
+  /* Optional cudaEvent_t handles recorded on `stream` immediately before and
+   * after the main decode kernel (for kernel-only timing); may be null. */
+  void* event_before;
+  void* event_after;
+} pab200_decode_args;
+
+/* Bytes of workspace pab200_decode() needs for these arguments on the
+ * current device (0 if the arguments are invalid; see pab200_last_error()).
+ * Replaces the partial-buffer allocations of src/kernel_triton.py:232-243. */
+size_t pab200_decode_workspace_size(const pab200_decode_args* args);
+
+/* Paged-attention decode.  Replaces flash_attn_with_kvcache_wrapper_triton
+ * (src/kernel_triton.py:181-307: planner + split kernel + reduce kernel) with
+ * two launches on `stream`: a device-side planner (no host sync) and one
+ * fused split-KV + log-sum-exp-merge kernel.  `workspace` is a device buffer
+ * of at least pab200_decode_workspace_size() bytes, 256-byte aligned; its
+ * contents need no initialisation.  `stream` is a cudaStream_t (0 = legacy
+ * default stream). */
+int pab200_decode(const pab200_decode_args* args, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* The north-star signature paged_attention(out, query, key_cache,
+ * value_cache, block_tables, context_lens, scale, block_size) over the
+ * reference page layout: out/query [num_seqs, num_q_heads, head_size]
+ * contiguous, caches [num_pages, block_size, head_size] contiguous,
+ * block_tables [num_seqs, num_kv_heads, max_blocks] contiguous int32,
+ * context_lens [num_seqs, num_kv_heads] contiguous int32.  Same semantics
+ * and workspace rules as pab200_decode(). */
+int pab200_paged_attention(void* out, const void* query, const void* key_cache,
+                           const void* value_cache, const int32_t* block_tables,
+                           const int32_t* context_lens, float scale,
+                           int32_t block_size, int32_t dtype, int32_t num_seqs,
+                           int32_t num_q_heads, int32_t num_kv_heads,
+                           int32_t head_size, int32_t max_blocks,
+                           int64_t num_pages, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Merge num_states partial attention states (o, lse) into `out`, the
+ * log-sum-exp combination of src/kernel_triton.py:120-174 applied across
+ * devices: out[r] = sum_i exp(lse_i[r] - LSE[r]) o_i[r], LSE[r] =
+ * log sum_i exp(lse_i[r]); rows whose states are all empty give zeros.
+ * state_o: [num_states, rows, head_size] fp32 contiguous; state_lse:
+ * [num_states, rows] fp32; out: [rows, head_size] with row stride
+ * out_stride_row (elements), type out_dtype (BF16, F16 or F32). */
+int pab200_merge_states(const float* state_o, const float* state_lse,
+                        int32_t num_states, int64_t rows, int32_t head_size,
+                        void* out, int64_t out_stride_row, int32_t out_dtype,
+                        void* stream);
+
+/* Copy the device status word of `workspace` (the PAB200_STATUS_* bits raised
+ * by the most recent pab200_decode call on it) to *status_out.  Synchronises
+ * `stream`. */
+int pab200_read_status(const void* workspace, uint32_t* status_out,
+                       void* stream);
+
+/* Static text for a pab200_status code. */
+const char* pab200_strerror(int status);
+
+/* Detail of the last failed call on this thread ("" if none). */
+const char* pab200_last_error(void);
+
+/* PAB200_ABI_VERSION of the loaded library. */
+int pab200_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAB200_H_ */

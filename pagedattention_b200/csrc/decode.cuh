@@ -1,0 +1,715 @@
+// Paged-attention decode kernels for sm_100a.
+//
+// Reference path (lashhw/pagedattention):
+//   planner        src/kernel_triton.py:206-243  (host, with a device sync)
+//   split kernel   src/kernel_triton.py:8-117    (one program per chunk x q head)
+//   reduce kernel  src/kernel_triton.py:120-174  (log-sum-exp merge of chunks)
+//   numerics       src/kernel_eager.py:29-56     (softmax(q K^T * scale) V)
+//
+// Design here:
+//   plan_kernel    one CTA.  Clamps every sequence length, prefix-sums the
+//                  page counts of all (sequence, kv head) pairs ("heads" below)
+//                  into `cum`, and gives every warp of the decode grid its
+//                  first head.  Heads of length 0 get their zero output here.
+//   decode_kernel  persistent.  The concatenation of all heads' pages is cut
+//                  into W equal contiguous ranges, one per warp (W = every
+//                  resident warp on the device), so the load is balanced to a
+//                  page whatever the length mix.  Each warp streams its pages
+//                  through a private ring of shared-memory stages filled by
+//                  tensor-map bulk copies (TMA, 128-byte swizzle, mbarrier
+//                  completion), computes S^T = K Q^T and O^T += V^T P^T with
+//                  mma.sync m16n8k16 (tokens are the M dimension, the G query
+//                  heads of one kv head the N dimension, so one K/V read
+//                  serves the whole group) and keeps an online softmax in
+//                  registers.  A head covered by one warp is written directly;
+//                  a head split over several warps has each warp write a
+//                  partial (max, sum, acc) and the last one to finish (atomic
+//                  ticket) merges them — the reduce kernel of the reference,
+//                  fused.
+//
+// Shared-memory stage layout (per warp, per ring slot), ST tokens:
+//   K: [D/64 planes][ST rows][128 bytes], then V with the same shape.
+//   A plane holds 64 consecutive head-dim elements of every token; its
+//   128-byte rows are 128B-swizzled by the TMA unit (16-byte chunk c of row r
+//   is stored at chunk c ^ (r % 8)), which makes every ldmatrix below
+//   bank-conflict free.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace pab {
+
+constexpr int kMaxDepth = 8;                      // ring slots per warp (max)
+constexpr int kMaxWarpsPerCta = 8;                // keeps 255 registers/thread
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per pipeline wait
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr uint32_t kStatusBadPage = 0x1u;
+constexpr uint32_t kStatusClamp = 0x2u;
+constexpr uint32_t kStatusNegative = 0x4u;
+constexpr uint32_t kStatusTimeout = 0x8u;
+constexpr int kMetaBytesPerSlot = 32;  // two int4 per ring slot
+
+struct DecodeParams {
+  void* out;
+  const void* q;
+  const int32_t* lens;
+  const int32_t* bt;
+  int64_t q_sb, q_sh, o_sb, o_sh, l_sb, l_sh, bt_sb, bt_sh, bt_si;
+  int32_t bt_mul, bt_add;
+  int32_t B, Hkv, G, D, bs, maxb;
+  int64_t num_pages;
+  int32_t head_in_map;  // NHD layout: kv head is the tensor map's y coordinate
+  float scale_log2;     // softmax_scale * log2(e)
+  int32_t total_warps;  // W
+  int32_t depth;        // ring slots per warp
+  // workspace
+  int32_t* cum;       // [n_heads + 1] exclusive prefix of page counts
+  int32_t* wstart;    // [W] first head of each warp's page range
+  uint32_t* tickets;  // [n_heads] arrivals of split heads (reset by planner)
+  uint32_t* status;   // [1] PAB200_STATUS_* bits
+  int32_t* weff;      // [1] warps in use: min(total_warps, total pages)
+  float* part;        // [(n_heads + W) * slot_floats] partial states
+  int32_t slot_floats;
+  // cross-device state output (optional)
+  float* state_o;
+  float* state_lse;
+};
+
+// The warp that owns global page P (0 <= P < T).  Warp w owns pages
+// [floor(w*T/W), floor((w+1)*T/W)).
+__device__ __forceinline__ int warp_of_page(int64_t P, int64_t T, int W) {
+  return static_cast<int>(((P + 1) * W - 1) / T);
+}
+
+template <typename T>
+__device__ __forceinline__ T from_float(float x);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <>
+__device__ __forceinline__ __half from_float<__half>(float x) {
+  return __float2half_rn(x);
+}
+
+// --------------------------------------------------------------------------
+// Planner: one CTA of 1024 threads.
+template <typename T>
+__global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_heads = p.B * p.Hkv;
+  const int cap = p.maxb * p.bs;
+  const int Hq = p.Hkv * p.G;
+  if (tid == 0) {
+    carry = 0;
+    *p.status = 0u;
+  }
+  __syncthreads();
+  uint32_t flags = 0;
+  for (int base = 0; base < n_heads; base += 1024) {
+    const int hd = base + tid;
+    int pages = 0;
+    if (hd < n_heads) {
+      const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+      int L = p.lens[s * p.l_sb + h * p.l_sh];
+      if (L < 0) {
+        flags |= kStatusNegative;
+        L = 0;
+      } else if (L > cap) {
+        flags |= kStatusClamp;
+        L = cap;
+      }
+      pages = (L + p.bs - 1) / p.bs;
+      p.tickets[hd] = 0u;
+    }
+    int x = pages;  // inclusive scan within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int v = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      warp_tot[lane] = v;
+    }
+    __syncthreads();
+    if (hd < n_heads)
+      p.cum[hd] = carry + (warp ? warp_tot[warp - 1] : 0) + x - pages;
+    __syncthreads();
+    if (tid == 0) carry += warp_tot[31];
+    __syncthreads();
+  }
+  if (flags) atomicOr(p.status, flags);
+  if (tid == 0) p.cum[n_heads] = carry;
+  __syncthreads();
+
+  // With more warps than pages some warps would own no page and the span
+  // count of a head (warp_of_page(last) - warp_of_page(first) + 1) would
+  // include them; capping W at the page count gives every warp >= 1 page.
+  const int64_t total = carry;
+  const int W = static_cast<int>(total < p.total_warps ? total : p.total_warps);
+  if (tid == 0) *p.weff = W;
+  for (int hd = tid; hd < n_heads; hd += 1024) {
+    const int64_t c0 = p.cum[hd], c1 = p.cum[hd + 1];
+    if (c1 > c0) {
+      // warps whose first page lies in [c0, c1)
+      const int64_t wa = (c0 * W + total - 1) / total;
+      const int64_t wb = (c1 * W + total - 1) / total;
+      for (int64_t w = wa; w < wb; ++w) p.wstart[w] = hd;
+    } else {
+      // Empty head: its output is zero (an empty state in state mode),
+      // matching softmax over zero keys times an empty V in
+      // src/kernel_eager.py:51-53.
+      const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+      for (int g = 0; g < p.G; ++g) {
+        const int qh = h * p.G + g;
+        if (p.state_o) {
+          float* o = p.state_o + (static_cast<int64_t>(s) * Hq + qh) * p.D;
+          for (int d = 0; d < p.D; ++d) o[d] = 0.f;
+          p.state_lse[static_cast<int64_t>(s) * Hq + qh] = -INFINITY;
+        } else {
+          T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh;
+          for (int d = 0; d < p.D; ++d) o[d] = from_float<T>(0.f);
+        }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Decode kernel.  T: element type; D: head size; NT: query-head tiles of 8
+// (G <= 8*NT); ST: tokens per ring stage.
+template <typename T, int D, int NT, int ST>
+__global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                  const __grid_constant__ CUtensorMap vmap,
+                  const DecodeParams p) {
+  constexpr int NH = D / 64;           // 128-byte planes per token row
+  constexpr int MT = ST / 16;          // 16-token MMA tiles per stage
+  constexpr int KS = D / 16;           // k-steps of QK^T == d-tiles of PV
+  constexpr int PLANE = ST * 128;      // bytes of one plane of one stage
+  constexpr int KV_BYTES = NH * PLANE;  // K (or V) bytes per stage
+  constexpr int STAGE_BYTES = 2 * KV_BYTES;
+  constexpr int GP = NT * 8;  // padded query-group size
+  static_assert(D % 64 == 0 && ST % 16 == 0, "shape");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  const uint32_t smem_base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (smem_base - raw_addr);
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int wpc = blockDim.x >> 5;
+  const int depth = p.depth;
+  const int gw = blockIdx.x * wpc + warp;
+  const int W = *p.weff;  // min(total_warps, total pages), set by the planner
+  if (gw >= W) return;
+
+  const int n_heads = p.B * p.Hkv;
+  const int64_t total = p.cum[n_heads];
+  if (total == 0) return;
+  const int64_t gs = static_cast<int64_t>(gw) * total / W;
+  const int64_t ge = static_cast<int64_t>(gw + 1) * total / W;
+  if (gs >= ge) return;
+
+  const int G = p.G, Hkv = p.Hkv, bs = p.bs;
+  const int pps = ST / bs;  // pages per stage
+  const uint32_t ring = smem_base + warp * depth * STAGE_BYTES;
+  uint8_t* tail = smem + wpc * depth * STAGE_BYTES;
+  const uint32_t bars = smem_addr(tail) + warp * kMaxDepth * 8;
+  int4* meta = reinterpret_cast<int4*>(tail + wpc * kMaxDepth * 8) +
+               warp * kMaxDepth * 2;
+  float* scratch = reinterpret_cast<float*>(
+                       tail + wpc * kMaxDepth * (8 + kMetaBytesPerSlot)) +
+                   warp * 2 * GP;
+
+  if (lane == 0) {
+    for (int i = 0; i < depth; ++i) mbar_init(bars + i * 8, 1);
+    fence_mbar_init();
+  }
+  if (lane == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  __syncwarp();
+  const uint64_t policy = l2_policy_evict_first();
+
+  // ------------------------------------------------ issue-side cursor state
+  // Window of 32 consecutive heads starting at `win`: lane i holds cum[win+i]
+  // and the clamped length of head win+i.
+  int win = 0;
+  int win_cum = 0, win_len = 0;
+  auto load_window = [&](int w0) {
+    win = w0;
+    const int hd = w0 + lane;
+    win_cum = (hd <= n_heads) ? p.cum[hd] : 0;
+    int L = 0;
+    if (hd < n_heads) {
+      const int s = hd / Hkv, h = hd - s * Hkv;
+      L = p.lens[s * p.l_sb + h * p.l_sh];
+      L = L < 0 ? 0 : (L > p.maxb * bs ? p.maxb * bs : L);
+    }
+    win_len = L;
+  };
+  int c_head = 0, c_lo = 0, c_hi = 0, c_len = 0, c_nspans = 0, c_wfirst = 0;
+  auto enter_head = [&](int hd) {
+    if (hd + 1 - win > 31) load_window(hd);
+    c_head = hd;
+    c_lo = __shfl_sync(0xffffffffu, win_cum, hd - win);
+    c_hi = __shfl_sync(0xffffffffu, win_cum, hd + 1 - win);
+    c_len = __shfl_sync(0xffffffffu, win_len, hd - win);
+    if (c_hi > c_lo) {
+      c_wfirst = warp_of_page(c_lo, total, W);
+      c_nspans = warp_of_page(c_hi - 1, total, W) - c_wfirst + 1;
+    }
+  };
+  load_window(p.wstart[gw]);
+  enter_head(win);
+
+  int64_t c_gp = gs;  // next global page to stage
+  // Next stage, prepared one issue ahead so its block-table loads overlap.
+  bool nx_valid = false;
+  int nx_head = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_nspans = 0,
+      nx_wfirst = 0;
+  int64_t nx_pid = 0;  // lane i < nx_np: page id of page i of the stage
+  auto prepare_next = [&]() {
+    if (c_gp >= ge) {
+      nx_valid = false;
+      return;
+    }
+    while (c_gp >= c_hi) enter_head(c_head + 1);
+    nx_valid = true;
+    nx_head = c_head;
+    nx_lp0 = static_cast<int>(c_gp - c_lo);
+    int np = pps;
+    if (c_hi - c_gp < np) np = static_cast<int>(c_hi - c_gp);
+    if (ge - c_gp < np) np = static_cast<int>(ge - c_gp);
+    nx_np = np;
+    nx_len = c_len;
+    nx_nspans = c_nspans;
+    nx_wfirst = c_wfirst;
+    if (lane < np) {
+      const int s = c_head / Hkv, h = c_head - s * Hkv;
+      const int32_t raw =
+          p.bt[s * p.bt_sb + h * p.bt_sh + static_cast<int64_t>(nx_lp0 + lane) * p.bt_si];
+      nx_pid = static_cast<int64_t>(raw) * p.bt_mul + static_cast<int64_t>(h) * p.bt_add;
+    }
+    c_gp += np;
+  };
+  auto issue = [&](int slot) -> bool {
+    if (!nx_valid) return false;
+    const uint32_t bar = bars + slot * 8;
+    if (lane == 0) {
+      meta[slot * 2] = make_int4(nx_head, nx_lp0, nx_np, nx_len);
+      meta[slot * 2 + 1] = make_int4(nx_nspans, nx_wfirst, 0, 0);
+      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nx_np * bs * D * 2 * 2));
+    }
+    __syncwarp();
+    const bool bad = lane < nx_np && (nx_pid < 0 || nx_pid >= p.num_pages);
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.status, kStatusBadPage);
+    // A rejected page id reads a box that lies wholly outside the tensor
+    // (negative row), which the TMA unit fills with zeros.
+    const int32_t row = bad ? -256 : static_cast<int32_t>(nx_pid * bs);
+    const int per_kv = pps * NH;
+    const int kv = lane / per_kv;
+    const int rem = lane - kv * per_kv;
+    const int pg = rem / NH;
+    const int hf = rem - pg * NH;
+    const int32_t zrow = __shfl_sync(0xffffffffu, row, pg & 31);
+    if (kv < 2 && pg < nx_np) {
+      const int h = nx_head % Hkv;
+      const uint32_t dst = ring + slot * STAGE_BYTES + kv * KV_BYTES +
+                           hf * PLANE + pg * bs * 128;
+      tma_load_3d(dst, kv ? &vmap : &kmap, hf * 64, p.head_in_map ? h : 0,
+                  zrow, bar, policy);
+    }
+    prepare_next();
+    return true;
+  };
+
+  // ------------------------------------------------ compute-side state
+  const int lr = lane >> 2;  // fragment row group
+  const int lc = lane & 3;   // fragment column pair
+  const int x7 = lane & 7;
+  const uint32_t k_lane = static_cast<uint32_t>(((lane & 7) + ((lane >> 3) & 1) * 8) * 128);
+  const int k_chunk = lane >> 4;
+  const uint32_t v_lane = static_cast<uint32_t>(((lane & 7) + (lane >> 4) * 8) * 128);
+  const int v_chunk = (lane >> 3) & 1;
+
+  uint32_t qb[KS][NT][2];
+  float acc[KS][NT][4];
+  float mrun[NT][2], lrun[NT][2];
+
+  auto start_head = [&](int hd) {
+    const int s = hd / Hkv, h = hd - s * Hkv;
+    const T* qp = static_cast<const T*>(p.q) + s * p.q_sb + static_cast<int64_t>(h) * G * p.q_sh;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int g = nt * 8 + lr;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t b0 = 0, b1 = 0;
+        if (g < G) {
+          const T* row = qp + g * p.q_sh + ks * 16 + lc * 2;
+          b0 = *reinterpret_cast<const uint32_t*>(row);
+          b1 = *reinterpret_cast<const uint32_t*>(row + 8);
+        }
+        qb[ks][nt][0] = b0;
+        qb[ks][nt][1] = b1;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        mrun[nt][e] = -INFINITY;
+        lrun[nt][e] = 0.f;
+      }
+#pragma unroll
+      for (int dt = 0; dt < KS; ++dt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[dt][nt][i] = 0.f;
+    }
+  };
+
+  // Merge the partial states of head `hd` written by warps
+  // [wfirst, wfirst + nspans) into its output (last arriver only).
+  auto merge_head = [&](int hd, int nspans, int wfirst) {
+    const int s = hd / Hkv, h = hd - s * Hkv;
+    const int Hq = Hkv * G;
+    const int sf = p.slot_floats;
+    const float* base = p.part + static_cast<int64_t>(hd + wfirst) * sf;
+    for (int g = lane; g < G; g += 32) {
+      float M = -INFINITY;
+#pragma unroll 4
+      for (int j = 0; j < nspans; ++j)
+        M = fmaxf(M, __ldcg(base + static_cast<int64_t>(j) * sf + G * D + g));
+      float L = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < nspans; ++j) {
+        const float* ps = base + static_cast<int64_t>(j) * sf;
+        L += fast_exp2(__ldcg(ps + G * D + g) - M) * __ldcg(ps + G * D + G + g);
+      }
+      scratch[g] = M;
+      scratch[GP + g] = L;
+    }
+    __syncwarp();
+    for (int e = lane; e < G * D / 4; e += 32) {
+      const int g = (e * 4) / D, d = (e * 4) - g * D;
+      const float M = scratch[g];
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int j = 0; j < nspans; ++j) {
+        const float* ps = base + static_cast<int64_t>(j) * sf;
+        const float w = fast_exp2(__ldcg(ps + G * D + g) - M);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(ps + g * D + d));
+        a.x += w * v.x;
+        a.y += w * v.y;
+        a.z += w * v.z;
+        a.w += w * v.w;
+      }
+      const float inv = 1.f / scratch[GP + g];
+      const int qh = h * G + g;
+      if (p.state_o) {
+        float4 o = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+        *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + d) = o;
+      } else {
+        T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + d;
+        const uint32_t lo = pack2<T>(a.x * inv, a.y * inv);
+        const uint32_t hi = pack2<T>(a.z * inv, a.w * inv);
+        *reinterpret_cast<uint2*>(o) = make_uint2(lo, hi);
+      }
+    }
+    if (p.state_o) {
+      for (int g = lane; g < G; g += 32)
+        p.state_lse[static_cast<int64_t>(s) * Hq + h * G + g] =
+            (scratch[g] + __log2f(scratch[GP + g])) * kLn2;
+    }
+    __syncwarp();
+  };
+
+  auto finish_head = [&](int hd, int nspans, int wfirst) {
+    float lt[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float l = lrun[nt][e];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        lt[nt][e] = l;
+      }
+    const int s = hd / Hkv, h = hd - s * Hkv;
+    const int Hq = Hkv * G;
+    if (nspans == 1) {
+      float inv[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) inv[nt][e] = 1.f / lt[nt][e];
+#pragma unroll
+      for (int dt = 0; dt < KS; ++dt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int g = nt * 8 + lc * 2 + (i & 1);
+            const int d = dt * 16 + lr + (i >> 1) * 8;
+            if (g < G) {
+              const float v = acc[dt][nt][i] * inv[nt][i & 1];
+              const int qh = h * G + g;
+              if (p.state_o)
+                p.state_o[(static_cast<int64_t>(s) * Hq + qh) * D + d] = v;
+              else
+                static_cast<T*>(p.out)[s * p.o_sb + qh * p.o_sh + d] = from_float<T>(v);
+            }
+          }
+      if (p.state_o && lr == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int g = nt * 8 + lc * 2 + e;
+            if (g < G)
+              p.state_lse[static_cast<int64_t>(s) * Hq + h * G + g] =
+                  (mrun[nt][e] + __log2f(lt[nt][e])) * kLn2;
+          }
+      }
+      return;
+    }
+    // Split head: publish this warp's partial, then take a ticket.
+    float* ps = p.part + static_cast<int64_t>(hd + gw) * p.slot_floats;
+#pragma unroll
+    for (int dt = 0; dt < KS; ++dt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int g = nt * 8 + lc * 2 + (i & 1);
+          const int d = dt * 16 + lr + (i >> 1) * 8;
+          if (g < G) __stcg(ps + g * D + d, acc[dt][nt][i]);
+        }
+    if (lr == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int g = nt * 8 + lc * 2 + e;
+          if (g < G) {
+            __stcg(ps + G * D + g, mrun[nt][e]);
+            __stcg(ps + G * D + G + g, lt[nt][e]);
+          }
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    uint32_t ticket = 0;
+    if (lane == 0) ticket = atomicAdd(p.tickets + hd, 1u);
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket == static_cast<uint32_t>(nspans - 1)) {
+      __threadfence();
+      merge_head(hd, nspans, wfirst);
+    }
+  };
+
+  // ------------------------------------------------ pipeline
+  prepare_next();
+  int issued = 0;
+  for (int i = 0; i < depth; ++i) {
+    if (!issue(i)) break;
+    ++issued;
+  }
+
+  int cur_head = -1, cur_nspans = 0, cur_wfirst = 0;
+  for (int it = 0; it < issued; ++it) {
+    const int slot = it % depth;
+    const int4 m0 = meta[slot * 2];
+    const int4 m1 = meta[slot * 2 + 1];
+    if (m0.x != cur_head) {
+      if (cur_head >= 0) finish_head(cur_head, cur_nspans, cur_wfirst);
+      cur_head = m0.x;
+      cur_nspans = m1.x;
+      cur_wfirst = m1.y;
+      start_head(cur_head);
+    }
+    const uint32_t bar = bars + slot * 8;
+    if (!mbar_wait(bar, static_cast<uint32_t>((it / depth) & 1), kWaitLimitNs)) {
+      if (lane == 0) atomicOr(p.status, kStatusTimeout);
+      for (int j = it + 1; j < issued; ++j)
+        mbar_wait(bars + (j % depth) * 8, static_cast<uint32_t>((j / depth) & 1),
+                  kWaitLimitNs);
+      return;
+    }
+    const int ntok_stage = m0.z * bs;
+    const int ntok_left = m0.w - m0.y * bs;
+    const int ntok = ntok_stage < ntok_left ? ntok_stage : ntok_left;
+    const int mtv = (ntok + 15) >> 4;
+    const uint32_t kbase = ring + slot * STAGE_BYTES;
+    const uint32_t vbase = kbase + KV_BYTES;
+
+    // S^T = K Q^T for the valid 16-token tiles.
+    float sc[MT][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[mt][nt][i] = 0.f;
+      if (mt < mtv) {
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t a[4];
+          const int c = (ks & 3) * 2 + k_chunk;
+          ldmatrix_x4(a, kbase + (ks >> 2) * PLANE + mt * 16 * 128 + k_lane +
+                             static_cast<uint32_t>((c ^ x7) << 4));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_16816<T>(sc[mt][nt], a, qb[ks][nt][0], qb[ks][nt][1]);
+        }
+      }
+    }
+    // Scale into log2 units and mask tokens past the valid range.
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = mt * 16 + lr + (i >> 1) * 8;
+          sc[mt][nt][i] = row < ntok ? sc[mt][nt][i] * p.scale_log2 : -INFINITY;
+        }
+    // Online softmax per query head (fragment column).
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) mx = fmaxf(mx, fmaxf(sc[mt][nt][e], sc[mt][nt][e + 2]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mnew = fmaxf(mrun[nt][e], mx);
+        const float alpha = fast_exp2(mrun[nt][e] - mnew);
+        mrun[nt][e] = mnew;
+        float ls = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const float p0 = fast_exp2(sc[mt][nt][e] - mnew);
+          const float p2 = fast_exp2(sc[mt][nt][e + 2] - mnew);
+          sc[mt][nt][e] = p0;
+          sc[mt][nt][e + 2] = p2;
+          ls += p0 + p2;
+        }
+        lrun[nt][e] = lrun[nt][e] * alpha + ls;
+#pragma unroll
+        for (int dt = 0; dt < KS; ++dt) {
+          acc[dt][nt][e] *= alpha;
+          acc[dt][nt][e + 2] *= alpha;
+        }
+      }
+    // P^T fragments (B operand of the PV product) by in-register transpose.
+    uint32_t pb[MT][NT][2];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        pb[mt][nt][0] = 0u;
+        pb[mt][nt][1] = 0u;
+        if (mt < mtv) {
+          pb[mt][nt][0] = movmatrix_trans(pack2<T>(sc[mt][nt][0], sc[mt][nt][1]));
+          pb[mt][nt][1] = movmatrix_trans(pack2<T>(sc[mt][nt][2], sc[mt][nt][3]));
+        }
+      }
+    // V rows past the valid range may hold stale or non-finite data; zero
+    // them so 0 * V stays 0.  (Whole 128-byte rows: swizzle-invariant.)
+    const bool dirty = ntok < mtv * 16;
+    if (dirty) {
+      const int nrows = mtv * 16 - ntok;
+      uint4* vz = reinterpret_cast<uint4*>(smem + (vbase - smem_base));
+      for (int idx = lane; idx < nrows * NH * 8; idx += 32) {
+        const int r = ntok + idx / (NH * 8);
+        const int rem = idx % (NH * 8);
+        const int hf = rem >> 3, ch = rem & 7;
+        vz[(hf * PLANE + r * 128) / 16 + ch] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+    // O^T += V^T P^T.
+#pragma unroll
+    for (int dt = 0; dt < KS; ++dt)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        if (mt < mtv) {
+          uint32_t a[4];
+          const int c = (dt & 3) * 2 + v_chunk;
+          ldmatrix_x4_trans(a, vbase + (dt >> 2) * PLANE + mt * 16 * 128 + v_lane +
+                                   static_cast<uint32_t>((c ^ x7) << 4));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_16816<T>(acc[dt][nt], a, pb[mt][nt][0], pb[mt][nt][1]);
+        }
+      }
+    __syncwarp();
+    if (dirty) {
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
+    if (issue(slot)) ++issued;
+  }
+  if (cur_head >= 0) finish_head(cur_head, cur_nspans, cur_wfirst);
+}
+
+// --------------------------------------------------------------------------
+// Cross-device merge of (o, lse) states: one warp per output row.
+template <typename TO>
+__device__ __forceinline__ void store_out4(TO* o, float4 v);
+template <>
+__device__ __forceinline__ void store_out4<float>(float* o, float4 v) {
+  *reinterpret_cast<float4*>(o) = v;
+}
+template <>
+__device__ __forceinline__ void store_out4<__nv_bfloat16>(__nv_bfloat16* o, float4 v) {
+  *reinterpret_cast<uint2*>(o) = make_uint2(pack2<__nv_bfloat16>(v.x, v.y), pack2<__nv_bfloat16>(v.z, v.w));
+}
+template <>
+__device__ __forceinline__ void store_out4<__half>(__half* o, float4 v) {
+  *reinterpret_cast<uint2*>(o) = make_uint2(pack2<__half>(v.x, v.y), pack2<__half>(v.z, v.w));
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(256) merge_states_kernel(
+    const float* __restrict__ so, const float* __restrict__ slse, int n,
+    int64_t rows, int D, TO* __restrict__ out, int64_t out_stride) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float M = -INFINITY;
+  for (int i = 0; i < n; ++i) M = fmaxf(M, slse[i * rows + row]);
+  for (int c = lane * 4; c < D; c += 128) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+    if (M != -INFINITY) {
+      for (int i = 0; i < n; ++i) {
+        const float w = fast_exp2((slse[i * rows + row] - M) * kLog2e);
+        const float4 v = *reinterpret_cast<const float4*>(so + (i * rows + row) * D + c);
+        a.x += w * v.x;
+        a.y += w * v.y;
+        a.z += w * v.z;
+        a.w += w * v.w;
+        L += w;
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    store_out4<TO>(out + row * out_stride + c, make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv));
+  }
+}
+
+}  // namespace pab

@@ -1,0 +1,452 @@
+// libpab200.so — host side of the C ABI declared in include/pab200.h.
+//
+// Replaces the host wrapper flash_attn_with_kvcache_wrapper_triton
+// (src/kernel_triton.py:181-307).  Differences by design: the chunk plan is
+// computed on the device (no .cpu() sync, no per-call H2D metadata copies,
+// src/kernel_triton.py:206-229), the partial buffers live in a caller-owned
+// workspace (no per-call allocation, :232-243), and the split and reduce
+// kernels are one launch.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "decode.cuh"
+#include "pab200.h"
+
+#define PAB200_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PAB200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+
+int device_sm_count(int dev) {
+  static int sms[kMaxDevices] = {0};
+  static std::mutex mu;
+  if (dev < 0 || dev >= kMaxDevices) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      sms[dev] = n;
+  }
+  return sms[dev];
+}
+
+int env_int(const char* name, int fallback) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return fallback;
+  return std::atoi(v);
+}
+
+// ------------------------------------------------------------------ kernels
+struct KernelOps {
+  void* fn;  // decode kernel (for attributes / occupancy)
+  cudaError_t (*launch)(dim3, dim3, size_t, cudaStream_t, const CUtensorMap&,
+                        const CUtensorMap&, const pab::DecodeParams&);
+};
+
+template <typename T, int D, int NT, int ST>
+cudaError_t launch_decode(dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                          const CUtensorMap& k, const CUtensorMap& v,
+                          const pab::DecodeParams& p) {
+  pab::decode_kernel<T, D, NT, ST><<<grid, block, smem, s>>>(k, v, p);
+  return cudaGetLastError();
+}
+
+template <typename T, int D, int NT, int ST>
+KernelOps ops_of() {
+  return KernelOps{reinterpret_cast<void*>(&pab::decode_kernel<T, D, NT, ST>),
+                   &launch_decode<T, D, NT, ST>};
+}
+
+template <typename T, int ST>
+bool select_dnt(int D, int nt, KernelOps* o) {
+  switch (D * 16 + nt) {
+    case 64 * 16 + 1: *o = ops_of<T, 64, 1, ST>(); return true;
+    case 64 * 16 + 2: *o = ops_of<T, 64, 2, ST>(); return true;
+    case 64 * 16 + 4: *o = ops_of<T, 64, 4, ST>(); return true;
+    case 128 * 16 + 1: *o = ops_of<T, 128, 1, ST>(); return true;
+    case 128 * 16 + 2: *o = ops_of<T, 128, 2, ST>(); return true;
+    case 256 * 16 + 1: *o = ops_of<T, 256, 1, ST>(); return true;
+    default: return false;
+  }
+}
+
+bool select_kernel(int dtype, int D, int nt, int st, KernelOps* o) {
+  if (dtype == PAB200_DTYPE_BF16)
+    return st == 32 ? select_dnt<__nv_bfloat16, 32>(D, nt, o)
+                    : select_dnt<__nv_bfloat16, 64>(D, nt, o);
+  return st == 32 ? select_dnt<__half, 32>(D, nt, o) : select_dnt<__half, 64>(D, nt, o);
+}
+
+// ------------------------------------------------------------------ planning
+struct Plan {
+  KernelOps ops;
+  int G, nt, st, wpc, depth, ctas_per_sm, grid, W;
+  size_t smem;
+  int n_heads;
+  int slot_floats;
+  size_t off_cum, off_wstart, off_tickets, off_part, ws_bytes;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool aligned(const void* p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+int validate(const pab200_decode_args* a) {
+  if (!a) return fail(PAB200_ERR_INVALID_ARGUMENT, "args is null");
+  if (a->dtype != PAB200_DTYPE_BF16 && a->dtype != PAB200_DTYPE_F16)
+    return fail(PAB200_ERR_UNSUPPORTED, "dtype %d: q/k/v must be bf16 or f16", a->dtype);
+  if (a->layout != PAB200_LAYOUT_PAGES && a->layout != PAB200_LAYOUT_NHD)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "unknown cache layout %d", a->layout);
+  if (a->num_seqs < 1 || a->num_kv_heads < 1 || a->num_q_heads < 1)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "num_seqs, num_q_heads, num_kv_heads must be >= 1");
+  if (a->num_q_heads % a->num_kv_heads != 0)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "num_q_heads (%d) %% num_kv_heads (%d) != 0",
+                a->num_q_heads, a->num_kv_heads);
+  const int D = a->head_size, bs = a->block_size;
+  if (D != 64 && D != 128 && D != 256)
+    return fail(PAB200_ERR_UNSUPPORTED, "head_size %d: supported 64, 128, 256", D);
+  if (bs != 8 && bs != 16 && bs != 32 && bs != 64)
+    return fail(PAB200_ERR_UNSUPPORTED, "block_size %d: supported 8, 16, 32, 64", bs);
+  const int G = a->num_q_heads / a->num_kv_heads;
+  if (G * D > 2048)
+    return fail(PAB200_ERR_UNSUPPORTED,
+                "query group %d x head_size %d exceeds the register tile (G*D <= 2048)", G, D);
+  if (a->max_blocks < 0 || a->num_pages < 0)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "max_blocks and num_pages must be >= 0");
+  const int64_t n_heads = int64_t(a->num_seqs) * a->num_kv_heads;
+  if (n_heads * (a->max_blocks > 0 ? a->max_blocks : 1) >= (int64_t(1) << 31) ||
+      int64_t(a->max_blocks) * bs >= (int64_t(1) << 31))
+    return fail(PAB200_ERR_UNSUPPORTED, "num_seqs*num_kv_heads*max_blocks too large (>= 2^31)");
+  if (a->num_pages * bs >= (int64_t(1) << 31))
+    return fail(PAB200_ERR_UNSUPPORTED, "num_pages*block_size too large (>= 2^31 rows)");
+  if (a->num_pages == 0 && a->max_blocks > 0)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "num_pages is 0 but max_blocks > 0");
+  if (!a->q || !a->seqlens) return fail(PAB200_ERR_INVALID_ARGUMENT, "q or seqlens is null");
+  if (!a->state_o && !a->out) return fail(PAB200_ERR_INVALID_ARGUMENT, "out is null");
+  if (a->state_o && !a->state_lse)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "state_o given without state_lse");
+  if (a->num_pages > 0 && (!a->k_cache || !a->v_cache || !a->block_table))
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "k_cache, v_cache or block_table is null");
+  if (!aligned(a->q, 4) || (a->q_stride_b & 1) || (a->q_stride_h & 1))
+    return fail(PAB200_ERR_ALIGNMENT, "q must be 4-byte aligned with even strides");
+  if (!a->state_o && (!aligned(a->out, 8) || (a->out_stride_b & 3) || (a->out_stride_h & 3)))
+    return fail(PAB200_ERR_ALIGNMENT, "out must be 8-byte aligned with strides that are multiples of 4");
+  if (a->state_o && (!aligned(a->state_o, 16) || !aligned(a->state_lse, 4)))
+    return fail(PAB200_ERR_ALIGNMENT, "state_o must be 16-byte aligned");
+  if (a->num_pages > 0 && (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16)))
+    return fail(PAB200_ERR_ALIGNMENT, "k_cache and v_cache must be 16-byte aligned");
+  if (a->num_splits < 0) return fail(PAB200_ERR_INVALID_ARGUMENT, "num_splits must be >= 0");
+  return PAB200_OK;
+}
+
+int make_plan(const pab200_decode_args* a, Plan* pl) {
+  int rc = validate(a);
+  if (rc) return rc;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const int sms = device_sm_count(dev);
+  if (sms <= 0) return fail(PAB200_ERR_CUDA, "cannot query the SM count of device %d", dev);
+
+  const int D = a->head_size, bs = a->block_size;
+  pl->G = a->num_q_heads / a->num_kv_heads;
+  pl->nt = pl->G <= 8 ? 1 : (pl->G <= 16 ? 2 : 4);
+  pl->st = bs <= 32 ? 32 : 64;
+  const int nh = D / 64;
+  if (2 * (pl->st / bs) * nh > 32)
+    return fail(PAB200_ERR_UNSUPPORTED, "block_size %d with head_size %d needs > 32 copies per stage", bs, D);
+  if (!select_kernel(a->dtype, D, pl->nt, pl->st, &pl->ops))
+    return fail(PAB200_ERR_UNSUPPORTED, "no kernel for head_size %d, group %d", D, pl->G);
+
+  const size_t stage = size_t(4) * pl->st * D;  // K + V bytes of one stage
+  int depth = stage <= 8192 ? 4 : (stage <= 32768 ? 3 : 2);
+  depth = env_int("PAB200_DEPTH", depth);
+  if (depth < 2 || depth > pab::kMaxDepth)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_DEPTH must be in [2, %d]", pab::kMaxDepth);
+  int wpc = static_cast<int>((200u * 1024u) / (depth * stage));
+  wpc = wpc < 1 ? 1 : (wpc > pab::kMaxWarpsPerCta ? pab::kMaxWarpsPerCta : wpc);
+  wpc = env_int("PAB200_WPC", wpc);
+  if (wpc < 1 || wpc > pab::kMaxWarpsPerCta)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_WPC must be in [1, %d]", pab::kMaxWarpsPerCta);
+  pl->depth = depth;
+  pl->wpc = wpc;
+  pl->smem = 1024 + size_t(wpc) * depth * stage +
+             size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + 2 * pl->nt * 8 * 4);
+  if (pl->smem > 232448)
+    return fail(PAB200_ERR_UNSUPPORTED, "shared memory %zu exceeds 227 KiB", pl->smem);
+
+  e = cudaFuncSetAttribute(pl->ops.fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(pl->smem));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pl->ops.fn, wpc * 32, pl->smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (per_sm < 1) return fail(PAB200_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
+  pl->ctas_per_sm = per_sm;
+  int W = sms * per_sm * wpc;
+  pl->n_heads = a->num_seqs * a->num_kv_heads;
+  if (a->num_splits > 1) {
+    const int64_t cap = int64_t(pl->n_heads) * a->num_splits;
+    if (cap < W) W = static_cast<int>(cap);
+  }
+  pl->W = W;
+  pl->grid = (W + wpc - 1) / wpc;
+
+  pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
+  size_t off = 256;  // status word
+  pl->off_cum = off;
+  off = align256(off + size_t(pl->n_heads + 1) * 4);
+  pl->off_wstart = off;
+  off = align256(off + size_t(W) * 4);
+  pl->off_tickets = off;
+  off = align256(off + size_t(pl->n_heads) * 4);
+  pl->off_part = off;
+  off = align256(off + size_t(pl->n_heads + W) * pl->slot_floats * 4);
+  pl->ws_bytes = off;
+  return PAB200_OK;
+}
+
+int encode_cache_map(const pab200_decode_args* a, const void* base, CUtensorMap* map) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(PAB200_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int D = a->head_size;
+  const uint64_t hc = a->layout == PAB200_LAYOUT_NHD ? uint64_t(a->num_kv_heads) : 1u;
+  cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(hc),
+                        cuuint64_t(a->num_pages) * cuuint64_t(a->block_size)};
+  cuuint64_t strides[2] = {cuuint64_t(D) * 2, cuuint64_t(hc) * D * 2};
+  cuuint32_t box[3] = {64, 1, cuuint32_t(a->block_size)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map,
+                   a->dtype == PAB200_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PAB200_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return PAB200_OK;
+}
+
+template <typename T>
+cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s) {
+  pab::plan_kernel<T><<<1, 1024, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+PAB200_EXPORT size_t pab200_decode_workspace_size(const pab200_decode_args* args) {
+  Plan pl;
+  if (make_plan(args, &pl) != PAB200_OK) return 0;
+  return pl.ws_bytes;
+}
+
+PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  Plan pl;
+  int rc = make_plan(a, &pl);
+  if (rc) return rc;
+  if (!workspace || workspace_bytes < pl.ws_bytes)
+    return fail(PAB200_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", pl.ws_bytes,
+                workspace ? workspace_bytes : size_t(0));
+  if (!aligned(workspace, 256)) return fail(PAB200_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+
+  pab::DecodeParams p{};
+  p.out = a->out;
+  p.q = a->q;
+  p.lens = a->seqlens;
+  p.bt = a->block_table;
+  p.q_sb = a->q_stride_b;
+  p.q_sh = a->q_stride_h;
+  p.o_sb = a->out_stride_b;
+  p.o_sh = a->out_stride_h;
+  p.l_sb = a->seqlens_stride_b;
+  p.l_sh = a->seqlens_stride_h;
+  p.bt_sb = a->bt_stride_b;
+  p.bt_sh = a->bt_stride_h;
+  p.bt_si = a->bt_stride_i;
+  p.bt_mul = a->bt_page_mul;
+  p.bt_add = a->bt_page_add;
+  p.B = a->num_seqs;
+  p.Hkv = a->num_kv_heads;
+  p.G = pl.G;
+  p.D = a->head_size;
+  p.bs = a->block_size;
+  p.maxb = a->max_blocks;
+  p.num_pages = a->num_pages;
+  p.head_in_map = a->layout == PAB200_LAYOUT_NHD ? 1 : 0;
+  p.scale_log2 = a->softmax_scale * pab::kLog2e;
+  p.total_warps = pl.W;
+  p.depth = pl.depth;
+  p.status = reinterpret_cast<uint32_t*>(ws);
+  p.weff = reinterpret_cast<int32_t*>(ws + 4);
+  p.cum = reinterpret_cast<int32_t*>(ws + pl.off_cum);
+  p.wstart = reinterpret_cast<int32_t*>(ws + pl.off_wstart);
+  p.tickets = reinterpret_cast<uint32_t*>(ws + pl.off_tickets);
+  p.part = reinterpret_cast<float*>(ws + pl.off_part);
+  p.slot_floats = pl.slot_floats;
+  p.state_o = a->state_o;
+  p.state_lse = a->state_lse;
+
+  CUtensorMap kmap, vmap;
+  if (a->num_pages > 0) {
+    if ((rc = encode_cache_map(a, a->k_cache, &kmap))) return rc;
+    if ((rc = encode_cache_map(a, a->v_cache, &vmap))) return rc;
+  } else {
+    // No pages: every sequence is empty, the planner writes all outputs and
+    // the decode kernel exits before touching the maps.
+    kmap = CUtensorMap{};
+    vmap = CUtensorMap{};
+  }
+
+  cudaError_t e = a->dtype == PAB200_DTYPE_BF16 ? launch_plan<__nv_bfloat16>(p, s)
+                                                 : launch_plan<__half>(p, s);
+  if (e != cudaSuccess) return cuda_fail(e, "plan kernel launch");
+  if (a->event_before) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_before), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  e = pl.ops.launch(dim3(pl.grid), dim3(pl.wpc * 32), pl.smem, s, kmap, vmap, p);
+  if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+  if (a->event_after) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_after), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  return PAB200_OK;
+}
+
+PAB200_EXPORT int pab200_paged_attention(void* out, const void* query, const void* key_cache,
+                                         const void* value_cache, const int32_t* block_tables,
+                                         const int32_t* context_lens, float scale,
+                                         int32_t block_size, int32_t dtype, int32_t num_seqs,
+                                         int32_t num_q_heads, int32_t num_kv_heads,
+                                         int32_t head_size, int32_t max_blocks, int64_t num_pages,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  pab200_decode_args a{};
+  a.out = out;
+  a.q = query;
+  a.k_cache = key_cache;
+  a.v_cache = value_cache;
+  a.seqlens = context_lens;
+  a.block_table = block_tables;
+  a.dtype = dtype;
+  a.layout = PAB200_LAYOUT_PAGES;
+  a.num_seqs = num_seqs;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_size = head_size;
+  a.block_size = block_size;
+  a.max_blocks = max_blocks;
+  a.num_pages = num_pages;
+  a.q_stride_b = int64_t(num_q_heads) * head_size;
+  a.q_stride_h = head_size;
+  a.out_stride_b = int64_t(num_q_heads) * head_size;
+  a.out_stride_h = head_size;
+  a.seqlens_stride_b = num_kv_heads;
+  a.seqlens_stride_h = 1;
+  a.bt_stride_b = int64_t(num_kv_heads) * max_blocks;
+  a.bt_stride_h = max_blocks;
+  a.bt_stride_i = 1;
+  a.bt_page_mul = 1;
+  a.bt_page_add = 0;
+  a.softmax_scale = scale;
+  a.num_splits = 0;
+  return pab200_decode(&a, workspace, workspace_bytes, stream);
+}
+
+PAB200_EXPORT int pab200_merge_states(const float* state_o, const float* state_lse,
+                                      int32_t num_states, int64_t rows, int32_t head_size,
+                                      void* out, int64_t out_stride_row, int32_t out_dtype,
+                                      void* stream) {
+  if (num_states < 1 || rows < 0 || head_size < 4 || (head_size & 3))
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "num_states >= 1, rows >= 0, head_size %% 4 == 0 required");
+  if (rows == 0) return PAB200_OK;
+  if (!state_o || !state_lse || !out) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  const size_t oal = out_dtype == PAB200_DTYPE_F32 ? 16 : 8;
+  if (!aligned(state_o, 16) || !aligned(out, oal) || (out_stride_row & 3))
+    return fail(PAB200_ERR_ALIGNMENT, "state_o 16-byte, out %zu-byte aligned, out_stride_row %% 4 == 0", oal);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>((rows + 7) / 8)), block(256);
+  switch (out_dtype) {
+    case PAB200_DTYPE_BF16:
+      pab::merge_states_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
+          state_o, state_lse, num_states, rows, head_size, static_cast<__nv_bfloat16*>(out), out_stride_row);
+      break;
+    case PAB200_DTYPE_F16:
+      pab::merge_states_kernel<__half><<<grid, block, 0, s>>>(
+          state_o, state_lse, num_states, rows, head_size, static_cast<__half*>(out), out_stride_row);
+      break;
+    case PAB200_DTYPE_F32:
+      pab::merge_states_kernel<float><<<grid, block, 0, s>>>(
+          state_o, state_lse, num_states, rows, head_size, static_cast<float*>(out), out_stride_row);
+      break;
+    default:
+      return fail(PAB200_ERR_UNSUPPORTED, "out_dtype %d", out_dtype);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+  return PAB200_OK;
+}
+
+PAB200_EXPORT int pab200_read_status(const void* workspace, uint32_t* status_out, void* stream) {
+  if (!workspace || !status_out) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(status_out, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the status word");
+  return PAB200_OK;
+}
+
+PAB200_EXPORT const char* pab200_strerror(int status) {
+  switch (status) {
+    case PAB200_OK: return "ok";
+    case PAB200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PAB200_ERR_UNSUPPORTED: return "unsupported configuration";
+    case PAB200_ERR_WORKSPACE: return "workspace missing or too small";
+    case PAB200_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case PAB200_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+PAB200_EXPORT const char* pab200_last_error(void) { return g_last_error; }
+
+PAB200_EXPORT int pab200_abi_version(void) { return PAB200_ABI_VERSION; }

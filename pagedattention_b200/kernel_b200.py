@@ -1,0 +1,321 @@
+"""B200 paged-attention decode: the Python face of libpab200.so.
+
+Public entry points:
+
+* ``flash_attn_with_kvcache_wrapper_b200(q, k_cache, v_cache, cache_seqlens,
+  block_table, softmax_scale, num_splits=1)`` — drop-in beside the reference's
+  ``flash_attn_with_kvcache_wrapper_{eager,triton,vllm}``
+  (src/kernel_eager.py:29, src/kernel_triton.py:181, src/kernel_vllm.py:4),
+  same keywords, shapes (src/common.py:1-14) and error types.
+* ``paged_attention(out, query, key_cache, value_cache, block_tables,
+  context_lens, scale, block_size)`` — the in-place form, which also accepts
+  vLLM-style [num_blocks, num_kv_heads, block_size, head_size] pools.
+* ``paged_attention_states`` / ``merge_states`` — the partial (o, lse) form and
+  its log-sum-exp merge, for contexts split across devices.
+
+Every call launches CUDA kernels from libpab200.so on the current stream of
+the tensors' device; there is no CPU or PyTorch fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import threading
+
+import torch
+
+from . import _lib
+from .common import _validate_decode_inputs
+
+_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
+
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_last_ws: dict[int, tuple[torch.Tensor, int]] = {}
+
+
+def _check_dtypes(q, k_cache, v_cache):
+    # The reference Triton wrapper raises TypeError on unsupported dtypes
+    # (src/kernel_triton.py:195-196); this kernel takes bf16 or fp16.
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"q must be bfloat16 or float16, got {q.dtype}")
+    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise TypeError("q, k_cache and v_cache must share one dtype "
+                        f"(got {q.dtype}, {k_cache.dtype}, {v_cache.dtype})")
+
+
+def _check_device(*tensors):
+    dev = tensors[0].device
+    if dev.type != "cuda":
+        raise ValueError("pagedattention_b200 runs on CUDA tensors only (no CPU fallback)")
+    for t in tensors[1:]:
+        if t.device != dev:
+            raise ValueError(f"all tensors must be on {dev}, got {t.device}")
+    return dev
+
+
+def _as_int32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype == torch.int32:
+        return t
+    if t.dtype in (torch.int64, torch.int16, torch.uint8, torch.int8):
+        return t.to(torch.int32)
+    raise TypeError(f"{name} must be an integer tensor, got {t.dtype}")
+
+
+def _workspace(lib, args, device, stream) -> torch.Tensor:
+    need = lib.pab200_decode_workspace_size(ctypes.byref(args))
+    if need == 0:
+        raise ValueError(f"pab200_decode_workspace_size: {lib.pab200_last_error().decode()}")
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(need, dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        _last_ws[device.index] = (ws, stream.cuda_stream)
+    return ws
+
+
+def _run_decode(args: _lib.DecodeArgs, device: torch.device) -> None:
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        ws = _workspace(lib, args, device, stream)
+        rc = lib.pab200_decode(ctypes.byref(args), ctypes.c_void_p(ws.data_ptr()),
+                               ws.numel(), ctypes.c_void_p(stream.cuda_stream))
+    if rc == _lib.ERR_INVALID_ARGUMENT or rc == _lib.ERR_UNSUPPORTED:
+        raise ValueError(f"pab200_decode: {_lib.error_text(lib, rc)}")
+    _lib.check(lib, rc, "pab200_decode")
+
+
+def _fill_common(args, *, q, k_cache, v_cache, lens, bt, dtype, B, Hq, Hkv, D, bs,
+                 num_pages, scale, num_splits):
+    args.q = q.data_ptr()
+    args.k_cache = k_cache.data_ptr()
+    args.v_cache = v_cache.data_ptr()
+    args.seqlens = lens.data_ptr()
+    args.block_table = bt.data_ptr()
+    args.dtype = _DTYPES[dtype]
+    args.num_seqs = B
+    args.num_q_heads = Hq
+    args.num_kv_heads = Hkv
+    args.head_size = D
+    args.block_size = bs
+    args.num_pages = num_pages
+    args.softmax_scale = float(scale)
+    args.num_splits = int(num_splits)
+
+
+def flash_attn_with_kvcache_wrapper_b200(q, k_cache, v_cache, cache_seqlens, block_table,
+                                         softmax_scale, num_splits=1):
+    """Paged decode attention; returns a new (batch, 1, Hq, head_size) tensor.
+
+    Arguments as in src/common.py:1-14: q (B, 1, Hq, D); k_cache, v_cache
+    (num_blocks, block_size, D), one page per (sequence, kv head); cache_seqlens
+    (B, Hkv); block_table (B, Hkv, max_num_blocks_per_head).  ``num_splits``
+    keeps the reference's meaning (src/kernel_triton.py:206-209, chunks per kv
+    head): 0 or 1 lets the kernel size the split to the device, n > 1 caps the
+    number of chunks at B*Hkv*n.
+    """
+    Hq, Hkv, G, D = _validate_decode_inputs(q, cache_seqlens, block_table)
+    _check_dtypes(q, k_cache, v_cache)
+    device = _check_device(q, k_cache, v_cache, cache_seqlens, block_table)
+    if k_cache.dim() != 3 or tuple(v_cache.shape) != tuple(k_cache.shape):
+        raise ValueError("k_cache and v_cache must both be (num_blocks, block_size, head_size)")
+    if k_cache.shape[2] != D:
+        raise ValueError(f"cache head_size {k_cache.shape[2]} != q head_size {D}")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("k_cache and v_cache must be contiguous")
+    if q.stride(3) != 1:
+        raise ValueError("q must be contiguous in head_size")
+    if num_splits < 0:
+        raise ValueError("num_splits must be >= 0")
+    B = q.shape[0]
+    lens = _as_int32(cache_seqlens, "cache_seqlens")
+    bt = _as_int32(block_table, "block_table")
+    out = torch.empty((B, 1, Hq, D), dtype=q.dtype, device=device)
+    args = _lib.DecodeArgs()
+    _fill_common(args, q=q, k_cache=k_cache, v_cache=v_cache, lens=lens, bt=bt, dtype=q.dtype,
+                 B=B, Hq=Hq, Hkv=Hkv, D=D, bs=k_cache.shape[1], num_pages=k_cache.shape[0],
+                 scale=softmax_scale, num_splits=num_splits)
+    args.out = out.data_ptr()
+    args.layout = _lib.LAYOUT_PAGES
+    args.max_blocks = bt.shape[2]
+    args.q_stride_b, args.q_stride_h = q.stride(0), q.stride(2)
+    args.out_stride_b, args.out_stride_h = out.stride(0), out.stride(2)
+    args.seqlens_stride_b, args.seqlens_stride_h = lens.stride(0), lens.stride(1)
+    args.bt_stride_b, args.bt_stride_h, args.bt_stride_i = bt.stride(0), bt.stride(1), bt.stride(2)
+    args.bt_page_mul, args.bt_page_add = 1, 0
+    _run_decode(args, device)
+    return out
+
+
+def _paged_args(query, key_cache, value_cache, block_tables, context_lens, scale, block_size,
+                kv_layout, num_splits):
+    """Shared argument handling of paged_attention / paged_attention_states."""
+    if query.dim() != 3:
+        raise ValueError("query must be (num_seqs, num_q_heads, head_size)")
+    _check_dtypes(query, key_cache, value_cache)
+    device = _check_device(query, key_cache, value_cache, block_tables, context_lens)
+    if tuple(key_cache.shape) != tuple(value_cache.shape):
+        raise ValueError("key_cache and value_cache shapes differ")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("key_cache and value_cache must be contiguous")
+    if query.stride(2) != 1:
+        raise ValueError("query must be contiguous in head_size")
+    B, Hq, D = query.shape
+    bt = _as_int32(block_tables, "block_tables")
+    lens = _as_int32(context_lens, "context_lens")
+    args = _lib.DecodeArgs()
+    if key_cache.dim() == 3:                       # reference page layout
+        if kv_layout not in ("HND", "pages"):
+            raise ValueError("a 3-D cache is (num_pages, block_size, head_size)")
+        if bt.dim() != 3:
+            raise ValueError("a 3-D (per-head page) cache needs block_tables "
+                             "(num_seqs, num_kv_heads, max_blocks)")
+        Hkv = bt.shape[1]
+        num_pages, bs, Dc = key_cache.shape
+        layout, mul, add = _lib.LAYOUT_PAGES, 1, 0
+    elif key_cache.dim() == 4 and kv_layout == "HND":  # [nb, Hkv, bs, D]
+        nb, Hkv, bs, Dc = key_cache.shape
+        num_pages = nb * Hkv
+        layout, mul, add = _lib.LAYOUT_PAGES, Hkv, 1
+    elif key_cache.dim() == 4 and kv_layout == "NHD":  # [nb, bs, Hkv, D]
+        nb, bs, Hkv, Dc = key_cache.shape
+        num_pages = nb
+        layout, mul, add = _lib.LAYOUT_NHD, 1, 0
+    else:
+        raise ValueError(f"unsupported cache rank {key_cache.dim()} / kv_layout {kv_layout!r}")
+    if Dc != D:
+        raise ValueError(f"cache head_size {Dc} != query head_size {D}")
+    if bs != block_size:
+        raise ValueError(f"block_size {block_size} != cache block size {bs}")
+    if Hq % Hkv != 0:
+        raise ValueError(f"num_q_heads {Hq} is not a multiple of num_kv_heads {Hkv}")
+    if bt.dim() == 3:
+        if bt.shape[0] != B or bt.shape[1] != Hkv:
+            raise ValueError("block_tables must be (num_seqs, num_kv_heads, max_blocks)")
+        sb, sh, si, maxb = bt.stride(0), bt.stride(1), bt.stride(2), bt.shape[2]
+    elif bt.dim() == 2:
+        if bt.shape[0] != B:
+            raise ValueError("block_tables must be (num_seqs, max_blocks)")
+        sb, sh, si, maxb = bt.stride(0), 0, bt.stride(1), bt.shape[1]
+    else:
+        raise ValueError("block_tables must be 2-D or 3-D")
+    if lens.dim() == 1 and lens.shape[0] == B:
+        lsb, lsh = lens.stride(0), 0
+    elif lens.dim() == 2 and tuple(lens.shape) == (B, Hkv):
+        lsb, lsh = lens.stride(0), lens.stride(1)
+    else:
+        raise ValueError("context_lens must be (num_seqs,) or (num_seqs, num_kv_heads)")
+    _fill_common(args, q=query, k_cache=key_cache, v_cache=value_cache, lens=lens, bt=bt,
+                 dtype=query.dtype, B=B, Hq=Hq, Hkv=Hkv, D=D, bs=bs, num_pages=num_pages,
+                 scale=scale, num_splits=num_splits)
+    args.layout = layout
+    args.max_blocks = maxb
+    args.q_stride_b, args.q_stride_h = query.stride(0), query.stride(1)
+    args.seqlens_stride_b, args.seqlens_stride_h = lsb, lsh
+    args.bt_stride_b, args.bt_stride_h, args.bt_stride_i = sb, sh, si
+    args.bt_page_mul, args.bt_page_add = mul, add
+    # keep converted tensors alive until the launch is enqueued
+    return args, device, (bt, lens)
+
+
+def paged_attention(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                    block_size, kv_layout="HND", num_splits=0):
+    """In-place paged decode: writes ``out`` (num_seqs, num_q_heads, head_size).
+
+    Caches: (num_pages, block_size, head_size) with block_tables
+    (num_seqs, num_kv_heads, max_blocks) — the reference layout; or a 4-D pool
+    (num_blocks, num_kv_heads, block_size, head_size) ("HND", default) or
+    (num_blocks, block_size, num_kv_heads, head_size) ("NHD") with block_tables
+    (num_seqs, max_blocks) of block ids shared by all kv heads.  context_lens:
+    (num_seqs,) or (num_seqs, num_kv_heads).
+    """
+    args, device, keep = _paged_args(query, key_cache, value_cache, block_tables, context_lens,
+                                     scale, block_size, kv_layout, num_splits)
+    if out.shape != query.shape or out.dtype != query.dtype or out.device != device:
+        raise ValueError("out must match query in shape, dtype and device")
+    if out.stride(2) != 1:
+        raise ValueError("out must be contiguous in head_size")
+    args.out = out.data_ptr()
+    args.out_stride_b, args.out_stride_h = out.stride(0), out.stride(1)
+    _run_decode(args, device)
+    del keep
+
+
+def paged_attention_states(query, key_cache, value_cache, block_tables, context_lens, scale,
+                           block_size, kv_layout="HND", num_splits=0):
+    """Like paged_attention, but return the partial state of the given KV range.
+
+    Returns (o, lse): o (num_seqs, num_q_heads, head_size) float32, the
+    attention output over just these tokens, and lse (num_seqs, num_q_heads)
+    float32, the natural log of the sum of exp(scaled score); empty ranges give
+    o = 0, lse = -inf.  ``merge_states`` combines states of disjoint ranges.
+    """
+    args, device, keep = _paged_args(query, key_cache, value_cache, block_tables, context_lens,
+                                     scale, block_size, kv_layout, num_splits)
+    B, Hq, D = query.shape
+    o = torch.empty((B, Hq, D), dtype=torch.float32, device=device)
+    lse = torch.empty((B, Hq), dtype=torch.float32, device=device)
+    args.state_o = o.data_ptr()
+    args.state_lse = lse.data_ptr()
+    _run_decode(args, device)
+    del keep
+    return o, lse
+
+
+def merge_states(state_o, state_lse, out=None, out_dtype=torch.bfloat16):
+    """Log-sum-exp merge of N partial states (the reduce of
+    src/kernel_triton.py:120-174, across devices).
+
+    state_o: (N, ..., head_size) float32; state_lse: (N, ...) float32.
+    Returns (or fills) out of shape (..., head_size).
+    """
+    if state_o.dtype != torch.float32 or state_lse.dtype != torch.float32:
+        raise TypeError("states must be float32")
+    device = _check_device(state_o, state_lse)
+    N, D = state_o.shape[0], state_o.shape[-1]
+    if tuple(state_lse.shape) != tuple(state_o.shape[:-1]):
+        raise ValueError("state_lse must be state_o.shape[:-1]")
+    rows = state_lse[0].numel()
+    so = state_o.contiguous()
+    sl = state_lse.contiguous()
+    if out is None:
+        out = torch.empty(tuple(state_o.shape[1:]), dtype=out_dtype, device=device)
+    code = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16,
+            torch.float32: _lib.DTYPE_F32}.get(out.dtype)
+    if code is None:
+        raise TypeError(f"unsupported out dtype {out.dtype}")
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous")
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        rc = lib.pab200_merge_states(ctypes.c_void_p(so.data_ptr()), ctypes.c_void_p(sl.data_ptr()),
+                                     N, rows, D, ctypes.c_void_p(out.data_ptr()), D, code,
+                                     ctypes.c_void_p(stream.cuda_stream))
+    _lib.check(lib, rc, "pab200_merge_states")
+    return out
+
+
+def read_status(device=None) -> int:
+    """PAB200_STATUS_* bits raised by the last decode call on ``device``
+    (synchronises that call's stream)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       torch.device(device).index or 0)
+    entry = _last_ws.get(dev.index)
+    if entry is None:
+        return 0
+    ws, stream_handle = entry
+    lib = _lib.load()
+    val = ctypes.c_uint32(0)
+    with torch.cuda.device(dev):
+        rc = lib.pab200_read_status(ctypes.c_void_p(ws.data_ptr()), ctypes.byref(val),
+                                    ctypes.c_void_p(stream_handle))
+    _lib.check(lib, rc, "pab200_read_status")
+    return int(val.value)
+
+
+def default_scale(head_size: int) -> float:
+    return 1.0 / math.sqrt(head_size)

@@ -1,0 +1,92 @@
+"""GPU parity of the sm_100a decode kernels against the fp32 oracle and the
+golden vectors produced by the reference's own eager implementation.
+
+Tolerance everywhere: torch.isclose(atol=2e-2, rtol=2e-2), the reference's
+parity bar (scripts/benchmark.py:63-72, 161).
+"""
+import pytest
+import torch
+
+from tests.util import (assert_close, golden_names, load_golden, random_case, run_oracle)
+
+pytestmark = pytest.mark.gpu
+
+
+def _b200():
+    from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200
+    return flash_attn_with_kvcache_wrapper_b200
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_vectors(cuda_device, name):
+    c = load_golden(name)
+    dev = cuda_device
+    out = _b200()(c["q"].to(dev), c["k_cache"].to(dev), c["v_cache"].to(dev),
+                  c["cache_seqlens"].to(dev), c["block_table"].to(dev), c["softmax_scale"],
+                  num_splits=1)
+    assert out.dtype == c["dtype"] and out.shape == c["q"].shape
+    assert_close(out, c["out_fp32"], what=name)
+
+
+CASES = [
+    # (B, Hkv, G, D, bs, dtype)
+    (3, 4, 1, 128, 16, torch.float16),
+    (2, 2, 2, 128, 16, torch.bfloat16),
+    (3, 2, 4, 128, 16, torch.bfloat16),
+    (2, 2, 8, 128, 32, torch.bfloat16),
+    (2, 2, 16, 128, 8, torch.bfloat16),
+    (2, 1, 32, 64, 8, torch.float16),
+    (2, 2, 12, 64, 16, torch.float16),
+    (2, 2, 3, 64, 64, torch.bfloat16),
+    (2, 2, 8, 256, 16, torch.bfloat16),
+    (2, 2, 2, 256, 64, torch.float16),
+]
+
+
+@pytest.mark.parametrize("B,Hkv,G,D,bs,dtype", CASES)
+def test_random_vs_oracle(cuda_device, B, Hkv, G, D, bs, dtype):
+    # lengths cover 0, 1, bs-1, bs, bs+1, stage boundaries and long heads
+    pool = [0, 1, bs - 1, bs, bs + 1, 31, 32, 33, 63, 64, 65, 200, 513, 1000]
+    lens = [[pool[(s * Hkv + h * 5 + D // 64) % len(pool)] for h in range(Hkv)]
+            for s in range(B)]
+    q, k, v, sl, bt, scale = random_case(B, Hkv, G, D, bs, lens, dtype, seed=B * 100 + G,
+                                         k_scale=4.0 if G == 32 else 1.0)
+    dev = cuda_device
+    out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
+    ref = run_oracle(q, k, v, sl, bt, scale)
+    assert_close(out, ref, what=f"B{B} Hkv{Hkv} G{G} D{D} bs{bs} {dtype}")
+
+
+@pytest.mark.parametrize("num_splits", [0, 1, 2, 7])
+def test_num_splits_same_result(cuda_device, num_splits):
+    q, k, v, sl, bt, scale = random_case(2, 3, 4, 128, 16, [[700, 5, 64], [0, 333, 1024]],
+                                         torch.bfloat16, seed=7)
+    dev = cuda_device
+    out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale,
+                  num_splits=num_splits)
+    ref = run_oracle(q, k, v, sl, bt, scale)
+    assert_close(out, ref, what=f"num_splits={num_splits}")
+
+
+def test_flattened_batch1_equals_batched(cuda_device):
+    """The reference's batch==1 flattened form gives the batched result."""
+    B, Hkv, G, D = 3, 2, 4, 128
+    q, k, v, sl, bt, scale = random_case(B, Hkv, G, D, 16, [[40, 100], [7, 0], [300, 16]],
+                                         torch.bfloat16, seed=11)
+    dev = cuda_device
+    f = _b200()
+    out_b = f(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
+    out_f = f(q.reshape(1, 1, B * Hkv * G, D).to(dev), k.to(dev), v.to(dev),
+              sl.reshape(1, B * Hkv).to(dev), bt.reshape(1, B * Hkv, -1).to(dev), scale)
+    assert torch.equal(out_b.reshape(1, 1, -1, D), out_f)
+
+
+def test_known_answers(cuda_device):
+    """seqlen 1 -> out equals the single V row; seqlen 0 -> zeros."""
+    q, k, v, sl, bt, scale = random_case(1, 2, 4, 128, 16, [[1, 0]], torch.bfloat16, seed=3)
+    dev = cuda_device
+    out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale).cpu()
+    page = int(bt[0, 0, 0])
+    for g in range(4):
+        assert torch.equal(out[0, 0, g], v[page, 0])
+    assert torch.count_nonzero(out[0, 0, 4:]) == 0
