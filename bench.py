@@ -1,0 +1,387 @@
+#!/usr/bin/env python
+"""Benchmark of the paged-attention decode path; prints ONE JSON line.
+
+    python bench.py [--gpus N --steps K --warmup W --workload NAME --impl b200|reference]
+
+N > 1 runs under torch.distributed.run, one rank per GPU.  A step is one
+decode call over one batch of the workload (default llama8b_gqa: 64 sequences
+x 4096 tokens, 32/8 heads, D 128, bs 16, bf16 — 1 GiB of KV, larger than the
+126 MB L2, so no flush is needed between steps).  Every rank decodes its own
+batch (seed + rank), so per-GPU work is fixed and the aggregate grows with N
+("weak" scaling); no collective is on the data path.
+
+value     KV-cache bytes read by all ranks / max-over-ranks device time of the K
+          steps (CUDA events around the public wrapper, inputs resident).
+roofline  algorithmic KV bytes per decode-kernel launch / the kernel's mean
+          event-timed duration, against the measured HBM copy bandwidth.
+e2e       the same metric through the public wrapper with the step's inputs
+          (query, cache_seqlens, block_table) copied from pinned host memory
+          and the output read back every step; the KV cache stays resident.
+--impl reference  the reference's CPU path (the fp32 eager restatement in
+          oracle/eager.py) on the host cores, on a bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "KV-cache read GB/s (% of B200 HBM peak) and µs per paged-decode call"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default="llama8b_gqa")
+    ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="wall budget of the CPU-baseline sample (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM-style copy)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
+
+
+def ncu_traffic(workload):
+    """DRAM bytes per decode-kernel launch from the committed ncu summary."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    try:
+        d = json.loads(p.read_text())[workload]
+        return d["dram_bytes_per_launch"], d.get("source")
+    except Exception:
+        return None, None
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons through NVML while the
+    timed region runs (read-only; nothing is set)."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, torch_device, period_s=0.02):
+        self.samples = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(torch_device)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(torch_device.index or 0)
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML missing: report no clocks
+            self.error = str(e)
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((time.time(), sm, reasons, power))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.handle is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.handle is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        sms = [s[1] for s in self.samples]
+        mask = 0
+        for s in self.samples:
+            mask |= s[2]
+        reasons = [k for k, v in self.REASONS.items() if mask & v and k != "gpu_idle"]
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sms),
+                "power_w_max": round(max(s[3] for s in self.samples), 1)}
+
+
+def cpu_oracle_sample(workload, seed, budget_s, threads):
+    """Time the fp32 CPU oracle on the first sequences of the workload.
+
+    Returns (GB/s over algorithmic KV bytes, description, cores)."""
+    import torch
+
+    from oracle import eager
+    from pagedattention_b200.workloads import make_inputs
+
+    # Calibrate on one sequence, then size the sample to the budget.
+    def run(nseq, reps):
+        inp = make_inputs(workload, seed=seed, num_seqs=nseq)
+        q, k, v, sl, bt = inp.reference_layout()
+        qn, kn, vn = q.float().numpy(), k.float().numpy(), v.float().numpy()
+        sln, btn = sl.numpy(), bt.numpy()
+        eager.flash_attn_with_kvcache(qn, kn, vn, sln, btn, inp.scale, threads=threads)  # warm
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            eager.flash_attn_with_kvcache(qn, kn, vn, sln, btn, inp.scale, threads=threads)
+        dt = (time.perf_counter() - t0) / reps
+        return inp.kv_bytes(), dt
+
+    nbytes, dt = run(1, 1)
+    per_seq = max(dt, 1e-4)
+    nseq = max(1, min(workload.num_seqs, int(budget_s / 3 / per_seq)))
+    reps = 3
+    nbytes, dt = run(nseq, reps)
+    desc = (f"first {nseq} of {workload.num_seqs} sequences of {workload.name} "
+            f"({nbytes / 1e6:.1f} MB of KV), fp32 eager oracle, {reps} timed reps")
+    del torch
+    return nbytes / dt / 1e9, desc, threads
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return  # the CPU reference arm runs on rank 0 only
+    import torch
+
+    from oracle import eager
+    from pagedattention_b200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS[args.workload]
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(cores)
+    # Size each step so warmup + steps finish in about two minutes.
+    budget_per_step = max(0.02, 120.0 / (args.steps + args.warmup))
+    inp1 = make_inputs(w, seed=args.seed, num_seqs=1)
+    q, k, v, sl, bt = inp1.reference_layout()
+    t0 = time.perf_counter()
+    eager.flash_attn_with_kvcache(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                  sl.numpy(), bt.numpy(), inp1.scale, threads=cores)
+    per_seq = max(time.perf_counter() - t0, 1e-4)
+    nseq = max(1, min(w.num_seqs, int(budget_per_step / per_seq)))
+    inp = make_inputs(w, seed=args.seed, num_seqs=nseq)
+    q, k, v, sl, bt = inp.reference_layout()
+    qn, kn, vn, sln, btn = q.float().numpy(), k.float().numpy(), v.float().numpy(), sl.numpy(), bt.numpy()
+    for _ in range(args.warmup):
+        eager.flash_attn_with_kvcache(qn, kn, vn, sln, btn, inp.scale, threads=cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eager.flash_attn_with_kvcache(qn, kn, vn, sln, btn, inp.scale, threads=cores)
+    dt = time.perf_counter() - t0
+    nbytes = inp.kv_bytes()
+    value = nbytes * args.steps / dt / 1e9
+    sample = (f"first {nseq} of {w.num_seqs} sequences of {w.name} per step "
+              f"({nbytes / 1e6:.1f} MB of KV), fp32 eager restatement (oracle/eager.py)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "description": w.description, "sample_seqs": nseq,
+                   "device": "cpu"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode
+    from pagedattention_b200.kernel_b200 import kernel_events
+    from pagedattention_b200.workloads import WORKLOADS, make_inputs
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    w = WORKLOADS[args.workload]
+    inp = make_inputs(w, seed=args.seed + rank, device=dev, gen_device=dev)
+    q, k, v, sl, bt = inp.reference_layout()
+    bt = bt.contiguous()
+    kv_bytes = inp.kv_bytes()
+    L2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    if kv_bytes <= 3 * L2:
+        raise SystemExit("workload KV fits in L2; this bench relies on inputs larger than L2")
+
+    def step():
+        return decode(q, k, v, sl, bt, inp.scale)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    kb = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ka = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for e in kb + ka:
+        e.record()  # create the events before the timed region
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev)
+    with sampler:
+        t_start.record()
+        for i in range(K):
+            with kernel_events(kb[i], ka[i]):
+                step()
+        t_end.record()
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    kernel_ms = statistics.fmean(b.elapsed_time(a) for b, a in zip(kb, ka))
+    kernel_ms = max_over_ranks(kernel_ms)
+    ms_per_step = elapsed_ms / K
+    value = kv_bytes * world * K / (elapsed_ms / 1e3) / 1e9
+
+    # e2e: per-step inputs from pinned host memory, output read back.
+    q_h = q.cpu().pin_memory()
+    sl_h = sl.cpu().pin_memory()
+    bt_h = bt.cpu().pin_memory()
+    q_d, sl_d, bt_d = torch.empty_like(q), torch.empty_like(sl), torch.empty_like(bt)
+    out_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        sl_d.copy_(sl_h, non_blocking=True)
+        bt_d.copy_(bt_h, non_blocking=True)
+        out = decode(q_d, k, v, sl_d, bt_d, inp.scale)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    E = max(1, min(args.e2e_steps, K))
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(E):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = kv_bytes * world * E / (e2e_ms / 1e3) / 1e9
+    h2d = q_h.numel() * q_h.element_size() + sl_h.numel() * 4 + bt_h.numel() * 4
+    d2h = out_h.numel() * out_h.element_size()
+
+    peak, peak_src = hbm_peak()
+    achieved = kv_bytes / (kernel_ms / 1e3) / 1e9
+    traffic, traffic_src = ncu_traffic(w.name)
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+            gbs, desc, used = cpu_oracle_sample(w, args.seed, args.cpu_seconds, cores)
+            cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": used, "kind": "port",
+                   "sample": desc}
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if q.dtype == torch.bfloat16 else "f16", "data": "synthetic",
+            "config": {"workload": w.name, "description": w.description,
+                       "num_seqs_per_gpu": w.num_seqs, "num_q_heads": w.num_q_heads,
+                       "num_kv_heads": w.num_kv_heads, "head_size": w.head_size,
+                       "block_size": w.block_size, "kv_bytes_per_gpu_step": kv_bytes,
+                       "parallelism": f"dp{world} (independent sequence batches, no collective)",
+                       "l2": f"inputs larger than L2 ({kv_bytes / 2**20:.0f} MiB KV per step "
+                             f"vs {L2 / 2**20:.0f} MiB L2), no flush"},
+            "us_per_call": round(ms_per_step * 1e3, 2),
+            "hbm_frac_of_measured_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "peak_source": peak_src,
+                         "kernel": "pab::decode_kernel", "kernel_us": round(kernel_ms * 1e3, 2),
+                         "algorithmic_bytes_per_launch": kv_bytes,
+                         "traffic_source": traffic_src},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": E,
+                    "note": "public wrapper; q, cache_seqlens, block_table H2D from pinned "
+                            "memory and the output D2H every step; KV cache resident"},
+            "clocks": sampler.summary(),
+            "gpu_launches": 2 * K,
+        }
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

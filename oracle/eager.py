@@ -105,7 +105,9 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens, block_table,
 
     items = [(s, h) for s in range(B) for h in range(Hkv)]
     if threads > 1:
-        with ThreadPoolExecutor(max_workers=threads) as ex:
+        # one BLAS thread per worker: nested BLAS threads oversubscribe the cores
+        from threadpoolctl import threadpool_limits
+        with threadpool_limits(1), ThreadPoolExecutor(max_workers=threads) as ex:
             list(ex.map(work, items))
     else:
         for it in items:

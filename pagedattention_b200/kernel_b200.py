@@ -21,6 +21,7 @@ from __future__ import annotations
 import ctypes
 import math
 import threading
+from contextlib import contextmanager
 
 import torch
 
@@ -29,6 +30,7 @@ from .common import _validate_decode_inputs
 
 _DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
 
+_tls = threading.local()
 _ws_lock = threading.Lock()
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 _last_ws: dict[int, tuple[torch.Tensor, int]] = {}
@@ -76,8 +78,25 @@ def _workspace(lib, args, device, stream) -> torch.Tensor:
     return ws
 
 
+@contextmanager
+def kernel_events(before: torch.cuda.Event, after: torch.cuda.Event):
+    """Record ``before``/``after`` around the main decode kernel of every
+    decode call made inside the block (kernel-only timing; both events must
+    already exist, i.e. have been recorded once)."""
+    prev = getattr(_tls, "events", None)
+    _tls.events = (before, after)
+    try:
+        yield
+    finally:
+        _tls.events = prev
+
+
 def _run_decode(args: _lib.DecodeArgs, device: torch.device) -> None:
     lib = _lib.load()
+    ev = getattr(_tls, "events", None)
+    if ev is not None:
+        args.event_before = ev[0].cuda_event
+        args.event_after = ev[1].cuda_event
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
         ws = _workspace(lib, args, device, stream)
