@@ -148,6 +148,37 @@ size_t pab200_decode_workspace_size(const pab200_decode_args* args);
 int pab200_decode(const pab200_decode_args* args, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Size of the fixed device scratch used by pab200_decode_noalloc(): 16 MiB. */
+#define PAB200_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* pab200_decode() for callers that cannot allocate device memory.  No
+ * counterpart in the reference.
+ *
+ * Some hosts of this library have no device allocator to hand a workspace
+ * from: a plain C or foreign-language binding with no CUDA memory manager of
+ * its own, or an engine whose pooling allocator has already reserved all free
+ * device memory, so that a fresh cudaMalloc would fail (and where cudaMalloc /
+ * cudaFree would also stall the device on every call).  This entry point takes
+ * the same arguments as pab200_decode() minus the workspace and uses instead a
+ * scratch array of PAB200_NOALLOC_SCRATCH_BYTES that is part of the library
+ * image: every GPU that loads the library holds it until the process exits.
+ * It calls no allocating routine.
+ *
+ * Limits and rules:
+ *  - Calls whose workspace (pab200_decode_workspace_size()) exceeds
+ *    PAB200_NOALLOC_SCRATCH_BYTES fail with PAB200_ERR_WORKSPACE; use
+ *    pab200_decode() with a caller workspace for those.
+ *  - The first call on a device, made with that device current, looks up the
+ *    scratch array's device address; make that first call before any stream
+ *    capture begins.
+ *  - All calls on a device share the one scratch array and it keeps the last
+ *    call's contents (the planner kernel of every call re-initialises the
+ *    parts that must start at zero), so calls that can overlap on the GPU
+ *    (different streams without ordering between them) race: serialise them.
+ *  - pab200_read_status() does not see this scratch; device status bits of
+ *    these calls are not reported. */
+int pab200_decode_noalloc(const pab200_decode_args* args, void* stream);
+
 /* The north-star signature paged_attention(out, query, key_cache,
  * value_cache, block_tables, context_lens, scale, block_size) over the
  * reference page layout: out/query [num_seqs, num_q_heads, head_size]

@@ -31,6 +31,9 @@ DTYPE_F32 = 2
 LAYOUT_PAGES = 0
 LAYOUT_NHD = 1
 
+# size of the fixed scratch of pab200_decode_noalloc
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
 # device status bits
 STATUS_BAD_PAGE_ID = 0x1
 STATUS_SEQLEN_CLAMP = 0x2
@@ -40,6 +43,7 @@ STATUS_WAIT_TIMEOUT = 0x8
 EXPORTED_SYMBOLS = (
     "pab200_decode_workspace_size",
     "pab200_decode",
+    "pab200_decode_noalloc",
     "pab200_paged_attention",
     "pab200_merge_states",
     "pab200_read_status",
@@ -110,6 +114,8 @@ def load() -> ctypes.CDLL:
     lib.pab200_decode_workspace_size.restype = ctypes.c_size_t
     lib.pab200_decode.argtypes = [P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.pab200_decode.restype = ctypes.c_int
+    lib.pab200_decode_noalloc.argtypes = [P, ctypes.c_void_p]
+    lib.pab200_decode_noalloc.restype = ctypes.c_int
     lib.pab200_paged_attention.argtypes = [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,

@@ -353,6 +353,49 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   return PAB200_OK;
 }
 
+// ---------------------------------------------------------------- no-alloc
+// Fixed scratch for callers that cannot provide a workspace (see
+// pab200_decode_noalloc in pab200.h).  In host code `g_noalloc_scratch` names
+// a host-side stand-in, not device memory: its device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[PAB200_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+int noalloc_scratch(void** out) {
+  static void* ptrs[kMaxDevices] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PAB200_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return PAB200_OK;
+}
+
+}  // namespace
+
+PAB200_EXPORT int pab200_decode_noalloc(const pab200_decode_args* a, void* stream) {
+  Plan pl;
+  int rc = make_plan(a, &pl);
+  if (rc) return rc;
+  if (pl.ws_bytes > PAB200_NOALLOC_SCRATCH_BYTES)
+    return fail(PAB200_ERR_WORKSPACE,
+                "this call needs %zu bytes of scratch but the fixed no-alloc scratch holds %u; "
+                "use pab200_decode with a caller workspace",
+                pl.ws_bytes, PAB200_NOALLOC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  if ((rc = noalloc_scratch(&ws))) return rc;
+  return pab200_decode(a, ws, PAB200_NOALLOC_SCRATCH_BYTES, stream);
+}
+
 PAB200_EXPORT int pab200_paged_attention(void* out, const void* query, const void* key_cache,
                                          const void* value_cache, const int32_t* block_tables,
                                          const int32_t* context_lens, float scale,
