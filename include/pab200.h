@@ -198,11 +198,14 @@ int pab200_paged_attention(void* out, const void* query, const void* key_cache,
 /* Merge num_states partial attention states (o, lse) into `out`, the
  * log-sum-exp combination of src/kernel_triton.py:120-174 applied across
  * devices: out[r] = sum_i exp(lse_i[r] - LSE[r]) o_i[r], LSE[r] =
- * log sum_i exp(lse_i[r]); rows whose states are all empty give zeros.
- * state_o: [num_states, rows, head_size] fp32 contiguous; state_lse:
- * [num_states, rows] fp32; out: [rows, head_size] with row stride
- * out_stride_row (elements), type out_dtype (BF16, F16 or F32). */
-int pab200_merge_states(const float* state_o, const float* state_lse,
+ * log sum_i exp(lse_i[r]); states with lse = -inf carry no weight and rows
+ * whose states are all empty give zeros.  State i's outputs are the fp32 rows
+ * state_o + i*o_stride ([rows, head_size], contiguous) and its log-sum-exps
+ * state_lse + i*lse_stride ([rows]); strides are in floats, o_stride a
+ * multiple of 4.  `out`: [rows, head_size] with row stride out_stride_row
+ * (elements), type out_dtype (BF16, F16 or F32). */
+int pab200_merge_states(const float* state_o, int64_t o_stride,
+                        const float* state_lse, int64_t lse_stride,
                         int32_t num_states, int64_t rows, int32_t head_size,
                         void* out, int64_t out_stride_row, int32_t out_dtype,
                         void* stream);

@@ -8,18 +8,22 @@ from .common import _validate_decode_inputs
 from .kernel_b200 import (
     default_scale,
     flash_attn_with_kvcache_wrapper_b200,
+    merge_packed_states,
     merge_states,
     paged_attention,
     paged_attention_states,
     read_status,
+    state_numel,
 )
 
 __all__ = [
     "_validate_decode_inputs",
     "default_scale",
     "flash_attn_with_kvcache_wrapper_b200",
+    "merge_packed_states",
     "merge_states",
     "paged_attention",
     "paged_attention_states",
     "read_status",
+    "state_numel",
 ]

@@ -123,8 +123,9 @@ def load() -> ctypes.CDLL:
         ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.pab200_paged_attention.restype = ctypes.c_int
     lib.pab200_merge_states.argtypes = [
-        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
-        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p]
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+        ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+        ctypes.c_void_p]
     lib.pab200_merge_states.restype = ctypes.c_int
     lib.pab200_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32),
                                        ctypes.c_void_p]

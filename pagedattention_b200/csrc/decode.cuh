@@ -188,20 +188,24 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
 
 // --------------------------------------------------------------------------
 // Decode kernel.  T: element type; D: head size; NT: query-head tiles of 8
-// (G <= 8*NT); ST: tokens per ring stage.
+// (G <= 8*NT); ST: tokens per ring stage (16, 32 or 64; a power of two
+// >= block_size).
 template <typename T, int D, int NT, int ST>
 __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     decode_kernel(const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap,
                   const DecodeParams p) {
-  constexpr int NH = D / 64;           // 128-byte planes per token row
-  constexpr int MT = ST / 16;          // 16-token MMA tiles per stage
-  constexpr int KS = D / 16;           // k-steps of QK^T == d-tiles of PV
-  constexpr int PLANE = ST * 128;      // bytes of one plane of one stage
+  constexpr int NH = D / 64;            // 128-byte planes per token row
+  constexpr int LOG2_NH = NH == 1 ? 0 : (NH == 2 ? 1 : 2);
+  constexpr int MT = ST / 16;           // 16-token MMA tiles per stage
+  constexpr int LOG2_ST = ST == 16 ? 4 : (ST == 32 ? 5 : 6);
+  constexpr int KS = D / 16;            // k-steps of QK^T == d-tiles of PV
+  constexpr int PLANE = ST * 128;       // bytes of one plane of one stage
   constexpr int KV_BYTES = NH * PLANE;  // K (or V) bytes per stage
   constexpr int STAGE_BYTES = 2 * KV_BYTES;
   constexpr int GP = NT * 8;  // padded query-group size
-  static_assert(D % 64 == 0 && ST % 16 == 0, "shape");
+  static_assert(D % 64 == 0 && (ST == 16 || ST == 32 || ST == 64), "shape");
+  static_assert(NH == 1 || NH == 2 || NH == 4, "head size");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -217,14 +221,18 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   if (gw >= W) return;
 
   const int n_heads = p.B * p.Hkv;
-  const int64_t total = p.cum[n_heads];
+  // Total pages < 2^31 (checked on the host), so page indices are 32-bit.
+  const int total = p.cum[n_heads];
   if (total == 0) return;
-  const int64_t gs = static_cast<int64_t>(gw) * total / W;
-  const int64_t ge = static_cast<int64_t>(gw + 1) * total / W;
+  const int gs = static_cast<int>(static_cast<int64_t>(gw) * total / W);
+  const int ge = static_cast<int>(static_cast<int64_t>(gw + 1) * total / W);
   if (gs >= ge) return;
 
   const int G = p.G, Hkv = p.Hkv, bs = p.bs;
-  const int pps = ST / bs;  // pages per stage
+  const int log2_bs = __ffs(bs) - 1;          // bs is a power of two
+  const int log2_pps = LOG2_ST - log2_bs;     // pages per stage = ST / bs
+  const int pps = 1 << log2_pps;
+  const int cap = p.maxb << log2_bs;
   const uint32_t ring = smem_base + warp * depth * STAGE_BYTES;
   uint8_t* tail = smem + wpc * depth * STAGE_BYTES;
   const uint32_t bars = smem_addr(tail) + warp * kMaxDepth * 8;
@@ -237,8 +245,6 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   if (lane == 0) {
     for (int i = 0; i < depth; ++i) mbar_init(bars + i * 8, 1);
     fence_mbar_init();
-  }
-  if (lane == 0) {
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
@@ -258,11 +264,14 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     if (hd < n_heads) {
       const int s = hd / Hkv, h = hd - s * Hkv;
       L = p.lens[s * p.l_sb + h * p.l_sh];
-      L = L < 0 ? 0 : (L > p.maxb * bs ? p.maxb * bs : L);
+      L = L < 0 ? 0 : (L > cap ? cap : L);
     }
     win_len = L;
   };
-  int c_head = 0, c_lo = 0, c_hi = 0, c_len = 0, c_nspans = 0, c_wfirst = 0;
+  // Current head of the issue cursor and what the stages of it need.
+  int c_head = 0, c_h = 0, c_lo = 0, c_hi = 0, c_len = 0, c_nspans = 0, c_wfirst = 0;
+  const int32_t* c_bt = p.bt;
+  int64_t c_pid_add = 0;
   auto enter_head = [&](int hd) {
     if (hd + 1 - win > 31) load_window(hd);
     c_head = hd;
@@ -270,6 +279,10 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     c_hi = __shfl_sync(0xffffffffu, win_cum, hd + 1 - win);
     c_len = __shfl_sync(0xffffffffu, win_len, hd - win);
     if (c_hi > c_lo) {
+      const int s = hd / Hkv;
+      c_h = hd - s * Hkv;
+      c_bt = p.bt + s * p.bt_sb + c_h * p.bt_sh;
+      c_pid_add = static_cast<int64_t>(c_h) * p.bt_add;
       c_wfirst = warp_of_page(c_lo, total, W);
       c_nspans = warp_of_page(c_hi - 1, total, W) - c_wfirst + 1;
     }
@@ -277,10 +290,10 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   load_window(p.wstart[gw]);
   enter_head(win);
 
-  int64_t c_gp = gs;  // next global page to stage
+  int c_gp = gs;  // next global page to stage
   // Next stage, prepared one issue ahead so its block-table loads overlap.
   bool nx_valid = false;
-  int nx_head = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_nspans = 0,
+  int nx_head = 0, nx_h = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_nspans = 0,
       nx_wfirst = 0;
   int64_t nx_pid = 0;  // lane i < nx_np: page id of page i of the stage
   auto prepare_next = [&]() {
@@ -291,20 +304,18 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     while (c_gp >= c_hi) enter_head(c_head + 1);
     nx_valid = true;
     nx_head = c_head;
-    nx_lp0 = static_cast<int>(c_gp - c_lo);
+    nx_h = c_h;
+    nx_lp0 = c_gp - c_lo;
     int np = pps;
-    if (c_hi - c_gp < np) np = static_cast<int>(c_hi - c_gp);
-    if (ge - c_gp < np) np = static_cast<int>(ge - c_gp);
+    if (c_hi - c_gp < np) np = c_hi - c_gp;
+    if (ge - c_gp < np) np = ge - c_gp;
     nx_np = np;
     nx_len = c_len;
     nx_nspans = c_nspans;
     nx_wfirst = c_wfirst;
-    if (lane < np) {
-      const int s = c_head / Hkv, h = c_head - s * Hkv;
-      const int32_t raw =
-          p.bt[s * p.bt_sb + h * p.bt_sh + static_cast<int64_t>(nx_lp0 + lane) * p.bt_si];
-      nx_pid = static_cast<int64_t>(raw) * p.bt_mul + static_cast<int64_t>(h) * p.bt_add;
-    }
+    if (lane < np)
+      nx_pid = static_cast<int64_t>(c_bt[static_cast<int64_t>(nx_lp0 + lane) * p.bt_si]) *
+                   p.bt_mul + c_pid_add;
     c_gp += np;
   };
   auto issue = [&](int slot) -> bool {
@@ -313,26 +324,24 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     if (lane == 0) {
       meta[slot * 2] = make_int4(nx_head, nx_lp0, nx_np, nx_len);
       meta[slot * 2 + 1] = make_int4(nx_nspans, nx_wfirst, 0, 0);
-      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nx_np * bs * D * 2 * 2));
+      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nx_np << (log2_bs + LOG2_NH + 8)));
     }
     __syncwarp();
     const bool bad = lane < nx_np && (nx_pid < 0 || nx_pid >= p.num_pages);
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.status, kStatusBadPage);
     // A rejected page id reads a box that lies wholly outside the tensor
     // (negative row), which the TMA unit fills with zeros.
-    const int32_t row = bad ? -256 : static_cast<int32_t>(nx_pid * bs);
-    const int per_kv = pps * NH;
-    const int kv = lane / per_kv;
-    const int rem = lane - kv * per_kv;
-    const int pg = rem / NH;
-    const int hf = rem - pg * NH;
-    const int32_t zrow = __shfl_sync(0xffffffffu, row, pg & 31);
+    const int32_t row = bad ? -256 : (static_cast<int32_t>(nx_pid) << log2_bs);
+    // lane -> (K or V, page of the stage, 64-column plane)
+    const int kv = lane >> (log2_pps + LOG2_NH);
+    const int pg = (lane >> LOG2_NH) & (pps - 1);
+    const int hf = lane & (NH - 1);
+    const int32_t zrow = __shfl_sync(0xffffffffu, row, pg);
     if (kv < 2 && pg < nx_np) {
-      const int h = nx_head % Hkv;
-      const uint32_t dst = ring + slot * STAGE_BYTES + kv * KV_BYTES +
-                           hf * PLANE + pg * bs * 128;
-      tma_load_3d(dst, kv ? &vmap : &kmap, hf * 64, p.head_in_map ? h : 0,
-                  zrow, bar, policy);
+      const uint32_t dst = ring + slot * STAGE_BYTES + kv * KV_BYTES + hf * PLANE +
+                           (pg << (log2_bs + 7));
+      tma_load_3d(dst, kv ? &vmap : &kmap, hf * 64, p.head_in_map ? nx_h : 0, zrow, bar,
+                  policy);
     }
     prepare_next();
     return true;
@@ -346,6 +355,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int k_chunk = lane >> 4;
   const uint32_t v_lane = static_cast<uint32_t>(((lane & 7) + (lane >> 4) * 8) * 128);
   const int v_chunk = (lane >> 3) & 1;
+  const float scale_log2 = p.scale_log2;
 
   uint32_t qb[KS][NT][2];
   float acc[KS][NT][4];
@@ -549,21 +559,26 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
                   kWaitLimitNs);
       return;
     }
-    const int ntok_stage = m0.z * bs;
-    const int ntok_left = m0.w - m0.y * bs;
+    const int ntok_stage = m0.z << log2_bs;
+    const int ntok_left = m0.w - (m0.y << log2_bs);
     const int ntok = ntok_stage < ntok_left ? ntok_stage : ntok_left;
     const int mtv = (ntok + 15) >> 4;
     const uint32_t kbase = ring + slot * STAGE_BYTES;
     const uint32_t vbase = kbase + KV_BYTES;
 
-    // S^T = K Q^T for the valid 16-token tiles.
+    // S^T = K Q^T for the valid 16-token tiles; even and odd k-steps go to
+    // separate accumulators so the two MMA dependency chains overlap.
     float sc[MT][NT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
+      float s2[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sc[mt][nt][i] = 0.f;
+        for (int i = 0; i < 4; ++i) {
+          sc[mt][nt][i] = 0.f;
+          s2[nt][i] = 0.f;
+        }
       if (mt < mtv) {
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
@@ -572,21 +587,41 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
           ldmatrix_x4(a, kbase + (ks >> 2) * PLANE + mt * 16 * 128 + k_lane +
                              static_cast<uint32_t>((c ^ x7) << 4));
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_16816<T>(sc[mt][nt], a, qb[ks][nt][0], qb[ks][nt][1]);
+          for (int nt = 0; nt < NT; ++nt) {
+            if (ks & 1)
+              mma_16816<T>(s2[nt], a, qb[ks][nt][0], qb[ks][nt][1]);
+            else
+              mma_16816<T>(sc[mt][nt], a, qb[ks][nt][0], qb[ks][nt][1]);
+          }
         }
       }
-    }
-    // Scale into log2 units and mask tokens past the valid range.
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = mt * 16 + lr + (i >> 1) * 8;
-          sc[mt][nt][i] = row < ntok ? sc[mt][nt][i] * p.scale_log2 : -INFINITY;
-        }
+        for (int i = 0; i < 4; ++i) sc[mt][nt][i] += s2[nt][i];
+    }
+    // Scale into log2 units; mask tokens past the valid range (tail only).
+    if (ntok == ST) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sc[mt][nt][i] *= scale_log2;
+    } else {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int row = mt * 16 + lr + (i >> 1) * 8;
+            sc[mt][nt][i] = row < ntok ? sc[mt][nt][i] * scale_log2 : -INFINITY;
+          }
+    }
     // Online softmax per query head (fragment column).
+    float alpha[NT][2];
+    bool grew = false;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -597,8 +632,10 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float mnew = fmaxf(mrun[nt][e], mx);
-        const float alpha = fast_exp2(mrun[nt][e] - mnew);
+        const float mold = mrun[nt][e];
+        const float mnew = fmaxf(mold, mx);
+        grew |= mnew > mold;
+        alpha[nt][e] = fast_exp2(mold - mnew);
         mrun[nt][e] = mnew;
         float ls = 0.f;
 #pragma unroll
@@ -609,13 +646,17 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
           sc[mt][nt][e + 2] = p2;
           ls += p0 + p2;
         }
-        lrun[nt][e] = lrun[nt][e] * alpha + ls;
-#pragma unroll
-        for (int dt = 0; dt < KS; ++dt) {
-          acc[dt][nt][e] *= alpha;
-          acc[dt][nt][e + 2] *= alpha;
-        }
+        lrun[nt][e] = lrun[nt][e] * alpha[nt][e] + ls;
       }
+    // Rescale the accumulator only when some running max grew.
+    if (__any_sync(0xffffffffu, grew)) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int dt = 0; dt < KS; ++dt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[dt][nt][i] *= alpha[nt][i & 1];
+    }
     // P^T fragments (B operand of the PV product) by in-register transpose.
     uint32_t pb[MT][NT][2];
 #pragma unroll
@@ -636,9 +677,8 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       const int nrows = mtv * 16 - ntok;
       uint4* vz = reinterpret_cast<uint4*>(smem + (vbase - smem_base));
       for (int idx = lane; idx < nrows * NH * 8; idx += 32) {
-        const int r = ntok + idx / (NH * 8);
-        const int rem = idx % (NH * 8);
-        const int hf = rem >> 3, ch = rem & 7;
+        const int r = ntok + (idx >> (LOG2_NH + 3));
+        const int hf = (idx >> 3) & (NH - 1), ch = idx & 7;
         vz[(hf * PLANE + r * 128) / 16 + ch] = make_uint4(0u, 0u, 0u, 0u);
       }
       __syncwarp();
@@ -686,20 +726,21 @@ __device__ __forceinline__ void store_out4<__half>(__half* o, float4 v) {
 
 template <typename TO>
 __global__ void __launch_bounds__(256) merge_states_kernel(
-    const float* __restrict__ so, const float* __restrict__ slse, int n,
-    int64_t rows, int D, TO* __restrict__ out, int64_t out_stride) {
+    const float* __restrict__ so, int64_t o_stride, const float* __restrict__ slse,
+    int64_t lse_stride, int n, int64_t rows, int D, TO* __restrict__ out,
+    int64_t out_stride) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   float M = -INFINITY;
-  for (int i = 0; i < n; ++i) M = fmaxf(M, slse[i * rows + row]);
+  for (int i = 0; i < n; ++i) M = fmaxf(M, slse[i * lse_stride + row]);
   for (int c = lane * 4; c < D; c += 128) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     float L = 0.f;
     if (M != -INFINITY) {
       for (int i = 0; i < n; ++i) {
-        const float w = fast_exp2((slse[i * rows + row] - M) * kLog2e);
-        const float4 v = *reinterpret_cast<const float4*>(so + (i * rows + row) * D + c);
+        const float w = fast_exp2((slse[i * lse_stride + row] - M) * kLog2e);
+        const float4 v = *reinterpret_cast<const float4*>(so + i * o_stride + row * D + c);
         a.x += w * v.x;
         a.y += w * v.y;
         a.z += w * v.z;

@@ -106,10 +106,20 @@ bool select_dnt(int D, int nt, KernelOps* o) {
 }
 
 bool select_kernel(int dtype, int D, int nt, int st, KernelOps* o) {
-  if (dtype == PAB200_DTYPE_BF16)
-    return st == 32 ? select_dnt<__nv_bfloat16, 32>(D, nt, o)
-                    : select_dnt<__nv_bfloat16, 64>(D, nt, o);
-  return st == 32 ? select_dnt<__half, 32>(D, nt, o) : select_dnt<__half, 64>(D, nt, o);
+  if (dtype == PAB200_DTYPE_BF16) {
+    switch (st) {
+      case 16: return select_dnt<__nv_bfloat16, 16>(D, nt, o);
+      case 32: return select_dnt<__nv_bfloat16, 32>(D, nt, o);
+      case 64: return select_dnt<__nv_bfloat16, 64>(D, nt, o);
+      default: return false;
+    }
+  }
+  switch (st) {
+    case 16: return select_dnt<__half, 16>(D, nt, o);
+    case 32: return select_dnt<__half, 32>(D, nt, o);
+    case 64: return select_dnt<__half, 64>(D, nt, o);
+    default: return false;
+  }
 }
 
 // ------------------------------------------------------------------ planning
@@ -188,20 +198,28 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   const int D = a->head_size, bs = a->block_size;
   pl->G = a->num_q_heads / a->num_kv_heads;
   pl->nt = pl->G <= 8 ? 1 : (pl->G <= 16 ? 2 : 4);
-  pl->st = bs <= 32 ? 32 : 64;
+  // Tokens per ring stage: a power of two >= block_size.
+  pl->st = env_int("PAB200_ST", bs <= 32 ? 32 : 64);
+  if ((pl->st != 16 && pl->st != 32 && pl->st != 64) || pl->st < bs)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_ST must be 16, 32 or 64 and >= block_size");
   const int nh = D / 64;
   if (2 * (pl->st / bs) * nh > 32)
     return fail(PAB200_ERR_UNSUPPORTED, "block_size %d with head_size %d needs > 32 copies per stage", bs, D);
   if (!select_kernel(a->dtype, D, pl->nt, pl->st, &pl->ops))
     return fail(PAB200_ERR_UNSUPPORTED, "no kernel for head_size %d, group %d", D, pl->G);
 
+  // Each warp owns a private ring of `depth` stages.  Throughput grows with
+  // resident warps (each warp's stage loop is latency-bound), so the default
+  // is a 2-deep ring and as many warps as ~200 KB of shared memory per SM
+  // holds (6 warps at 16 KiB stages).
   const size_t stage = size_t(4) * pl->st * D;  // K + V bytes of one stage
-  int depth = stage <= 8192 ? 4 : (stage <= 32768 ? 3 : 2);
-  depth = env_int("PAB200_DEPTH", depth);
+  int depth = env_int("PAB200_DEPTH", 2);
   if (depth < 2 || depth > pab::kMaxDepth)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_DEPTH must be in [2, %d]", pab::kMaxDepth);
-  int wpc = static_cast<int>((200u * 1024u) / (depth * stage));
-  wpc = wpc < 1 ? 1 : (wpc > pab::kMaxWarpsPerCta ? pab::kMaxWarpsPerCta : wpc);
+  int warps_per_sm = static_cast<int>((200u * 1024u) / (depth * stage));
+  if (warps_per_sm < 1) warps_per_sm = 1;
+  int wpc = warps_per_sm;
+  while (wpc > pab::kMaxWarpsPerCta) wpc = (wpc + 1) / 2;
   wpc = env_int("PAB200_WPC", wpc);
   if (wpc < 1 || wpc > pab::kMaxWarpsPerCta)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_WPC must be in [1, %d]", pab::kMaxWarpsPerCta);
@@ -435,7 +453,8 @@ PAB200_EXPORT int pab200_paged_attention(void* out, const void* query, const voi
   return pab200_decode(&a, workspace, workspace_bytes, stream);
 }
 
-PAB200_EXPORT int pab200_merge_states(const float* state_o, const float* state_lse,
+PAB200_EXPORT int pab200_merge_states(const float* state_o, int64_t o_stride,
+                                      const float* state_lse, int64_t lse_stride,
                                       int32_t num_states, int64_t rows, int32_t head_size,
                                       void* out, int64_t out_stride_row, int32_t out_dtype,
                                       void* stream) {
@@ -443,23 +462,30 @@ PAB200_EXPORT int pab200_merge_states(const float* state_o, const float* state_l
     return fail(PAB200_ERR_INVALID_ARGUMENT, "num_states >= 1, rows >= 0, head_size %% 4 == 0 required");
   if (rows == 0) return PAB200_OK;
   if (!state_o || !state_lse || !out) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  if (num_states > 1 && (o_stride < rows * head_size || lse_stride < rows))
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "state strides smaller than one state");
   const size_t oal = out_dtype == PAB200_DTYPE_F32 ? 16 : 8;
-  if (!aligned(state_o, 16) || !aligned(out, oal) || (out_stride_row & 3))
-    return fail(PAB200_ERR_ALIGNMENT, "state_o 16-byte, out %zu-byte aligned, out_stride_row %% 4 == 0", oal);
+  if (!aligned(state_o, 16) || (o_stride & 3) || !aligned(out, oal) || (out_stride_row & 3))
+    return fail(PAB200_ERR_ALIGNMENT,
+                "state_o 16-byte aligned with o_stride %% 4 == 0, out %zu-byte aligned, "
+                "out_stride_row %% 4 == 0", oal);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>((rows + 7) / 8)), block(256);
   switch (out_dtype) {
     case PAB200_DTYPE_BF16:
       pab::merge_states_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
-          state_o, state_lse, num_states, rows, head_size, static_cast<__nv_bfloat16*>(out), out_stride_row);
+          state_o, o_stride, state_lse, lse_stride, num_states, rows, head_size,
+          static_cast<__nv_bfloat16*>(out), out_stride_row);
       break;
     case PAB200_DTYPE_F16:
       pab::merge_states_kernel<__half><<<grid, block, 0, s>>>(
-          state_o, state_lse, num_states, rows, head_size, static_cast<__half*>(out), out_stride_row);
+          state_o, o_stride, state_lse, lse_stride, num_states, rows, head_size,
+          static_cast<__half*>(out), out_stride_row);
       break;
     case PAB200_DTYPE_F32:
       pab::merge_states_kernel<float><<<grid, block, 0, s>>>(
-          state_o, state_lse, num_states, rows, head_size, static_cast<float*>(out), out_stride_row);
+          state_o, o_stride, state_lse, lse_stride, num_states, rows, head_size,
+          static_cast<float*>(out), out_stride_row);
       break;
     default:
       return fail(PAB200_ERR_UNSUPPORTED, "out_dtype %d", out_dtype);

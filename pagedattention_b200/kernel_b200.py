@@ -175,7 +175,6 @@ def _paged_args(query, key_cache, value_cache, block_tables, context_lens, scale
     if query.dim() != 3:
         raise ValueError("query must be (num_seqs, num_q_heads, head_size)")
     _check_dtypes(query, key_cache, value_cache)
-    device = _check_device(query, key_cache, value_cache, block_tables, context_lens)
     if tuple(key_cache.shape) != tuple(value_cache.shape):
         raise ValueError("key_cache and value_cache shapes differ")
     if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
@@ -227,6 +226,7 @@ def _paged_args(query, key_cache, value_cache, block_tables, context_lens, scale
         lsb, lsh = lens.stride(0), lens.stride(1)
     else:
         raise ValueError("context_lens must be (num_seqs,) or (num_seqs, num_kv_heads)")
+    device = _check_device(query, key_cache, value_cache, bt, lens)
     _fill_common(args, q=query, k_cache=key_cache, v_cache=value_cache, lens=lens, bt=bt,
                  dtype=query.dtype, B=B, Hq=Hq, Hkv=Hkv, D=D, bs=bs, num_pages=num_pages,
                  scale=scale, num_splits=num_splits)
@@ -263,25 +263,57 @@ def paged_attention(out, query, key_cache, value_cache, block_tables, context_le
     del keep
 
 
+def state_numel(num_seqs: int, num_q_heads: int, head_size: int) -> int:
+    """Floats in one packed partial state: o [rows, D] then lse [rows], the lse
+    part padded to a multiple of 4 floats (rows = num_seqs * num_q_heads)."""
+    rows = num_seqs * num_q_heads
+    return rows * head_size + ((rows + 3) // 4) * 4
+
+
 def paged_attention_states(query, key_cache, value_cache, block_tables, context_lens, scale,
-                           block_size, kv_layout="HND", num_splits=0):
+                           block_size, kv_layout="HND", num_splits=0, state=None):
     """Like paged_attention, but return the partial state of the given KV range.
 
     Returns (o, lse): o (num_seqs, num_q_heads, head_size) float32, the
     attention output over just these tokens, and lse (num_seqs, num_q_heads)
     float32, the natural log of the sum of exp(scaled score); empty ranges give
-    o = 0, lse = -inf.  ``merge_states`` combines states of disjoint ranges.
+    o = 0, lse = -inf.  ``state``, if given, is a float32 tensor of
+    ``state_numel(...)`` elements that receives the packed (o, lse) (the layout
+    ``merge_packed_states`` reads).  ``merge_states`` combines states of
+    disjoint ranges.
     """
     args, device, keep = _paged_args(query, key_cache, value_cache, block_tables, context_lens,
                                      scale, block_size, kv_layout, num_splits)
     B, Hq, D = query.shape
-    o = torch.empty((B, Hq, D), dtype=torch.float32, device=device)
-    lse = torch.empty((B, Hq), dtype=torch.float32, device=device)
+    rows = B * Hq
+    if state is None:
+        state = torch.empty(state_numel(B, Hq, D), dtype=torch.float32, device=device)
+    if (state.dtype != torch.float32 or state.numel() < state_numel(B, Hq, D)
+            or not state.is_contiguous() or state.device != device):
+        raise ValueError("state must be a contiguous float32 tensor of state_numel() elements")
+    o = state[:rows * D].view(B, Hq, D)
+    lse = state[rows * D:rows * D + rows].view(B, Hq)
     args.state_o = o.data_ptr()
     args.state_lse = lse.data_ptr()
     _run_decode(args, device)
     del keep
     return o, lse
+
+
+def _merge(lib, device, o_ptr, o_stride, lse_ptr, lse_stride, n, rows, D, out):
+    code = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16,
+            torch.float32: _lib.DTYPE_F32}.get(out.dtype)
+    if code is None:
+        raise TypeError(f"unsupported out dtype {out.dtype}")
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous")
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        rc = lib.pab200_merge_states(ctypes.c_void_p(o_ptr), o_stride, ctypes.c_void_p(lse_ptr),
+                                     lse_stride, n, rows, D, ctypes.c_void_p(out.data_ptr()), D,
+                                     code, ctypes.c_void_p(stream.cuda_stream))
+    _lib.check(lib, rc, "pab200_merge_states")
+    return out
 
 
 def merge_states(state_o, state_lse, out=None, out_dtype=torch.bfloat16):
@@ -302,20 +334,27 @@ def merge_states(state_o, state_lse, out=None, out_dtype=torch.bfloat16):
     sl = state_lse.contiguous()
     if out is None:
         out = torch.empty(tuple(state_o.shape[1:]), dtype=out_dtype, device=device)
-    code = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16,
-            torch.float32: _lib.DTYPE_F32}.get(out.dtype)
-    if code is None:
-        raise TypeError(f"unsupported out dtype {out.dtype}")
-    if not out.is_contiguous():
-        raise ValueError("out must be contiguous")
-    lib = _lib.load()
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device)
-        rc = lib.pab200_merge_states(ctypes.c_void_p(so.data_ptr()), ctypes.c_void_p(sl.data_ptr()),
-                                     N, rows, D, ctypes.c_void_p(out.data_ptr()), D, code,
-                                     ctypes.c_void_p(stream.cuda_stream))
-    _lib.check(lib, rc, "pab200_merge_states")
-    return out
+    return _merge(_lib.load(), device, so.data_ptr(), rows * D, sl.data_ptr(), rows, N, rows, D,
+                  out)
+
+
+def merge_packed_states(states, num_seqs, num_q_heads, head_size, out=None,
+                        out_dtype=torch.bfloat16):
+    """Merge N packed states (rows of a (N, S) float32 tensor, S >=
+    state_numel(...), as written by ``paged_attention_states(state=...)`` and
+    gathered across devices) into out (num_seqs, num_q_heads, head_size)."""
+    if states.dtype != torch.float32 or states.dim() != 2 or not states.is_contiguous():
+        raise ValueError("states must be a contiguous float32 (N, S) tensor")
+    device = _check_device(states)
+    N, S = states.shape
+    rows = num_seqs * num_q_heads
+    if S < state_numel(num_seqs, num_q_heads, head_size) or S % 4:
+        raise ValueError("state row too short or not a multiple of 4 floats")
+    if out is None:
+        out = torch.empty((num_seqs, num_q_heads, head_size), dtype=out_dtype, device=device)
+    base = states.data_ptr()
+    return _merge(_lib.load(), device, base, S, base + rows * head_size * 4, S, N, rows,
+                  head_size, out)
 
 
 def read_status(device=None) -> int:
