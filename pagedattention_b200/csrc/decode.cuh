@@ -187,6 +187,68 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
 }
 
 // --------------------------------------------------------------------------
+// Merge helpers.  (m, l) pairs are running maxima (log2 units) and sums of
+// 2^(score - m); combining folds the second pair into the first.  An empty
+// pair has m = -inf, l = 0.
+__device__ __forceinline__ void sm_combine(float& m, float& l, float m2, float l2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;  // both empty
+  l = l * fast_exp2(m - mn) + l2 * fast_exp2(m2 - mn);
+  m = mn;
+}
+
+// acc[k] = sum over spans j of 2^(m_j[g] - M[g]) * acc_j[g][d..d+3] for K of
+// this lane's float4 output elements, e = lane + 32 * (k0 + k) (g = 4e / D,
+// d = 4e % D), loading SB spans x K elements per batch so that 16 loads are
+// in flight.  M[g] is read from scratch[g].  Elements past the output
+// (e >= G*D/4) read slot offset 0 and are not stored by the caller.
+template <int K>
+__device__ __forceinline__ void merge_accumulate(const float* base, int sf, int nspans, int G,
+                                                 int D, int lane, int k0, const float* scratch,
+                                                 float4 (&acc)[K]) {
+  constexpr int SB = 16 / K;
+  const int e4 = G * D / 4;
+  int off[K], goff[K];
+  float Mg[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int e = lane + 32 * (k0 + k);
+    const int g = e < e4 ? (e * 4) / D : 0;
+    off[k] = e < e4 ? e * 4 : 0;  // g*D + d == 4e
+    goff[k] = G * D + g;
+    Mg[k] = scratch[g];
+    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int j0 = 0; j0 < nspans; j0 += SB) {
+    float4 v[SB][K];
+    float mm[SB][K];
+#pragma unroll
+    for (int b = 0; b < SB; ++b) {
+      const int j = j0 + b < nspans ? j0 + b : nspans - 1;
+      const float* ps = base + static_cast<int64_t>(j) * sf;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        v[b][k] = __ldcg(reinterpret_cast<const float4*>(ps + off[k]));
+        mm[b][k] = __ldcg(ps + goff[k]);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < SB; ++b) {
+      if (j0 + b < nspans) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const float w = fast_exp2(mm[b][k] - Mg[k]);
+          acc[k].x += w * v[b][k].x;
+          acc[k].y += w * v[b][k].y;
+          acc[k].z += w * v[b][k].z;
+          acc[k].w += w * v[b][k].w;
+        }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
 // Decode kernel.  T: element type; D: head size; NT: query-head tiles of 8
 // (G <= 8*NT); ST: tokens per ring stage (16, 32 or 64; a power of two
 // >= block_size).
@@ -391,41 +453,57 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   };
 
   // Merge the partial states of head `hd` written by warps
-  // [wfirst, wfirst + nspans) into its output (last arriver only).
+  // [wfirst, wfirst + nspans) into its output (last arriver only).  The merge
+  // sits on the critical path of the head's last warp, so both passes keep
+  // many loads in flight: pass 1 strides the lanes over the spans and
+  // combines (max, sum) pairs across lanes; pass 2 accumulates each lane's
+  // output elements over batches of spans loaded together.
   auto merge_head = [&](int hd, int nspans, int wfirst) {
     const int s = hd / Hkv, h = hd - s * Hkv;
     const int Hq = Hkv * G;
     const int sf = p.slot_floats;
     const float* base = p.part + static_cast<int64_t>(hd + wfirst) * sf;
-    for (int g = lane; g < G; g += 32) {
-      float M = -INFINITY;
-#pragma unroll 4
-      for (int j = 0; j < nspans; ++j)
-        M = fmaxf(M, __ldcg(base + static_cast<int64_t>(j) * sf + G * D + g));
-      float L = 0.f;
-#pragma unroll 4
-      for (int j = 0; j < nspans; ++j) {
-        const float* ps = base + static_cast<int64_t>(j) * sf;
-        L += fast_exp2(__ldcg(ps + G * D + g) - M) * __ldcg(ps + G * D + G + g);
+    for (int g0 = 0; g0 < G; g0 += 8) {
+      float mx[8], sm[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mx[i] = -INFINITY;
+        sm[i] = 0.f;
       }
-      scratch[g] = M;
-      scratch[GP + g] = L;
+      for (int j = lane; j < nspans; j += 32) {
+        const float* ps = base + static_cast<int64_t>(j) * sf + G * D;
+        float mj[8], lj[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          mj[i] = g0 + i < G ? __ldcg(ps + g0 + i) : -INFINITY;
+          lj[i] = g0 + i < G ? __ldcg(ps + G + g0 + i) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sm_combine(mx[i], sm[i], mj[i], lj[i]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float om = __shfl_xor_sync(0xffffffffu, mx[i], o);
+          const float os = __shfl_xor_sync(0xffffffffu, sm[i], o);
+          sm_combine(mx[i], sm[i], om, os);
+        }
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (g0 + i < G) {
+            scratch[g0 + i] = mx[i];
+            scratch[GP + g0 + i] = sm[i];
+          }
+      }
     }
     __syncwarp();
-    for (int e = lane; e < G * D / 4; e += 32) {
+    const int e4 = G * D / 4;
+    const int per_lane = (e4 + 31) / 32;  // float4 output elements per lane
+    auto emit = [&](int e, const float4& a) {
+      if (e >= e4) return;
       const int g = (e * 4) / D, d = (e * 4) - g * D;
-      const float M = scratch[g];
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-      for (int j = 0; j < nspans; ++j) {
-        const float* ps = base + static_cast<int64_t>(j) * sf;
-        const float w = fast_exp2(__ldcg(ps + G * D + g) - M);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(ps + g * D + d));
-        a.x += w * v.x;
-        a.y += w * v.y;
-        a.z += w * v.z;
-        a.w += w * v.w;
-      }
       const float inv = 1.f / scratch[GP + g];
       const int qh = h * G + g;
       if (p.state_o) {
@@ -436,6 +514,23 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
         const uint32_t lo = pack2<T>(a.x * inv, a.y * inv);
         const uint32_t hi = pack2<T>(a.z * inv, a.w * inv);
         *reinterpret_cast<uint2*>(o) = make_uint2(lo, hi);
+      }
+    };
+    if (per_lane == 1) {
+      float4 a1[1];
+      merge_accumulate<1>(base, sf, nspans, G, D, lane, 0, scratch, a1);
+      emit(lane, a1[0]);
+    } else if (per_lane == 2) {
+      float4 a2[2];
+      merge_accumulate<2>(base, sf, nspans, G, D, lane, 0, scratch, a2);
+      emit(lane, a2[0]);
+      emit(lane + 32, a2[1]);
+    } else {
+      for (int k0 = 0; k0 < per_lane; k0 += 4) {
+        float4 a4[4];
+        merge_accumulate<4>(base, sf, nspans, G, D, lane, k0, scratch, a4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) emit(lane + 32 * (k0 + k), a4[k]);
       }
     }
     if (p.state_o) {
