@@ -113,6 +113,7 @@ def load() -> ctypes.CDLL:
     lib.pab200_decode_workspace_size.argtypes = [P]
     lib.pab200_decode_workspace_size.restype = ctypes.c_size_t
     lib.pab200_decode.argtypes = [P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    # plain Python ints are accepted for the pointer and size arguments
     lib.pab200_decode.restype = ctypes.c_int
     lib.pab200_decode_noalloc.argtypes = [P, ctypes.c_void_p]
     lib.pab200_decode_noalloc.restype = ctypes.c_int

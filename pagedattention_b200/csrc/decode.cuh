@@ -71,6 +71,9 @@ struct DecodeParams {
   int32_t* weff;      // [1] warps in use: min(total_warps, total pages)
   float* part;        // [(n_heads + W) * slot_floats] partial states
   int32_t slot_floats;
+  // 1: split heads only publish partials and reduce_kernel merges them;
+  // 0: the last warp to finish a split head merges it (atomic ticket).
+  int32_t merge_in_kernel;
   // cross-device state output (optional)
   float* state_o;
   float* state_lse;
@@ -615,6 +618,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
           }
         }
     }
+    if (p.merge_in_kernel) return;  // reduce_kernel merges after this kernel
     __threadfence();
     __syncwarp();
     uint32_t ticket = 0;
@@ -800,6 +804,104 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     if (issue(slot)) ++issued;
   }
   if (cur_head >= 0) finish_head(cur_head, cur_nspans, cur_wfirst);
+}
+
+// --------------------------------------------------------------------------
+// Reduce kernel: merges the partial states of every split head after the
+// decode kernel (the reduce of src/kernel_triton.py:120-174, planned on the
+// device).  One warp per output row (head, query head g): lanes stride over
+// the head's spans to form (max, sum), the per-span weights are kept in
+// registers and broadcast by shuffle, and each lane accumulates 4 head-dim
+// elements over batches of spans loaded together.
+template <typename T>
+__global__ void __launch_bounds__(256) reduce_kernel(const DecodeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int G = p.G, D = p.D;
+  const int n_heads = p.B * p.Hkv;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);  // hd * G + g
+  if (row >= n_heads * G) return;
+  const int hd = row / G, g = row - hd * G;
+  const int c0 = p.cum[hd], c1 = p.cum[hd + 1];
+  if (c1 <= c0) return;  // empty head: written by the planner
+  const int W = *p.weff;
+  const int total = p.cum[n_heads];
+  const int wfirst = warp_of_page(c0, total, W);
+  const int nspans = warp_of_page(c1 - 1, total, W) - wfirst + 1;
+  if (nspans == 1) return;  // written by the decode kernel
+  const int sf = p.slot_floats;
+  const float* base = p.part + static_cast<int64_t>(hd + wfirst) * sf;
+  // Spans j = lane + 32 r, r < 4, are this lane's; more than 128 spans per
+  // head fall back to reloading m from memory in the accumulation.
+  float mj[4], mx = -INFINITY, sm = 0.f;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int j = lane + 32 * r;
+    mj[r] = -INFINITY;
+    if (j < nspans) {
+      const float* ps = base + static_cast<int64_t>(j) * sf + G * D;
+      mj[r] = __ldcg(ps + g);
+      sm_combine(mx, sm, mj[r], __ldcg(ps + G + g));
+    }
+  }
+  for (int j = lane + 128; j < nspans; j += 32) {
+    const float* ps = base + static_cast<int64_t>(j) * sf + G * D;
+    sm_combine(mx, sm, __ldcg(ps + g), __ldcg(ps + G + g));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+    const float os = __shfl_xor_sync(0xffffffffu, sm, o);
+    sm_combine(mx, sm, om, os);
+  }
+  float wj[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) wj[r] = fast_exp2(mj[r] - mx);
+  const float inv = 1.f / sm;
+  const int Hq = p.Hkv * G;
+  const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+  const int qh = h * G + g;
+  const int iters = (D + 127) / 128;  // the same for every lane (shuffles below)
+  for (int it = 0; it < iters; ++it) {
+    const int c = lane * 4 + it * 128;
+    const bool active = c < D;
+    const int cc = active ? c : 0;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j0 = 0; j0 < nspans; j0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        const int j = j0 + b < nspans ? j0 + b : nspans - 1;
+        v[b] = __ldcg(reinterpret_cast<const float4*>(base + static_cast<int64_t>(j) * sf + g * D + cc));
+      }
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        const int j = j0 + b;
+        const int r = (j >> 5) & 3;  // warp-uniform
+        const float src = r == 0 ? wj[0] : (r == 1 ? wj[1] : (r == 2 ? wj[2] : wj[3]));
+        float w = __shfl_sync(0xffffffffu, src, j & 31);
+        if (j >= 128 && j < nspans)
+          w = fast_exp2(__ldcg(base + static_cast<int64_t>(j) * sf + G * D + g) - mx);
+        if (j < nspans) {
+          a.x += w * v[b].x;
+          a.y += w * v[b].y;
+          a.z += w * v[b].z;
+          a.w += w * v[b].w;
+        }
+      }
+    }
+    if (active) {
+      if (p.state_o) {
+        *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + c) =
+            make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+      } else {
+        T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + c;
+        *reinterpret_cast<uint2*>(o) =
+            make_uint2(pack2<T>(a.x * inv, a.y * inv), pack2<T>(a.z * inv, a.w * inv));
+      }
+    }
+  }
+  if (p.state_o && lane == 0)
+    p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (mx + __log2f(sm)) * kLn2;
 }
 
 // --------------------------------------------------------------------------

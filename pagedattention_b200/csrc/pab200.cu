@@ -126,6 +126,7 @@ bool select_kernel(int dtype, int D, int nt, int st, KernelOps* o) {
 struct Plan {
   KernelOps ops;
   int G, nt, st, wpc, depth, ctas_per_sm, grid, W;
+  int merge_in_kernel;
   size_t smem;
   int n_heads;
   int slot_floats;
@@ -186,6 +187,77 @@ int validate(const pab200_decode_args* a) {
   return PAB200_OK;
 }
 
+// Dynamic shared memory of one decode CTA: ring slots, then per-warp
+// mbarriers, stage records and merge scratch (see decode_kernel).
+size_t decode_smem(int wpc, int depth, size_t stage, int nt) {
+  return 1024 + size_t(wpc) * depth * stage +
+         size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + 2 * nt * 8 * 4);
+}
+
+struct Geometry {
+  int wpc, per_sm;
+  size_t smem;
+};
+
+// Warps per CTA and CTAs per SM for one decode kernel.  Each warp's stage
+// loop is latency-bound, so throughput follows the number of resident warps:
+// try every CTA size and keep the one with the most warps per SM (shared
+// memory and registers both limit it; ties go to the larger CTA).  Results
+// are cached per device, kernel, ring depth and stage size.
+int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, int nt, int forced_wpc,
+                    Geometry* out) {
+  struct Entry {
+    int dev;
+    void* fn;
+    int depth;
+    size_t stage;
+    int forced;
+    Geometry g;
+  };
+  static Entry cache[128];
+  static int used = 0;
+  static void* attr_set[kMaxDevices][64] = {{nullptr}};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].dev == dev && cache[i].fn == ops.fn && cache[i].depth == depth &&
+        cache[i].stage == stage && cache[i].forced == forced_wpc) {
+      *out = cache[i].g;
+      return PAB200_OK;
+    }
+  if (dev < 0 || dev >= kMaxDevices) return fail(PAB200_ERR_CUDA, "device index %d out of range", dev);
+  bool have_attr = false;
+  for (int i = 0; i < 64 && attr_set[dev][i]; ++i) have_attr |= attr_set[dev][i] == ops.fn;
+  if (!have_attr) {
+    cudaError_t e = cudaFuncSetAttribute(ops.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    for (int i = 0; i < 64; ++i)
+      if (!attr_set[dev][i]) {
+        attr_set[dev][i] = ops.fn;
+        break;
+      }
+  }
+  if (forced_wpc && (forced_wpc < 1 || forced_wpc > pab::kMaxWarpsPerCta))
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_WPC must be in [1, %d]", pab::kMaxWarpsPerCta);
+  static const int kCandidates[] = {8, 6, 4, 3, 2, 1};
+  const int* cand = forced_wpc ? &forced_wpc : kCandidates;
+  const int ncand = forced_wpc ? 1 : 6;
+  Geometry best{0, 0, 0};
+  for (int ci = 0; ci < ncand; ++ci) {
+    const int wpc = cand[ci];
+    const size_t smem = decode_smem(wpc, depth, stage, nt);
+    if (smem > 232448) continue;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops.fn, wpc * 32, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (per_sm * wpc > best.per_sm * best.wpc) best = Geometry{wpc, per_sm, smem};
+  }
+  if (best.per_sm < 1) return fail(PAB200_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
+  if (used < 128) cache[used++] = Entry{dev, ops.fn, depth, stage, forced_wpc, best};
+  *out = best;
+  return PAB200_OK;
+}
+
 int make_plan(const pab200_decode_args* a, Plan* pl) {
   int rc = validate(a);
   if (rc) return rc;
@@ -216,27 +288,13 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   int depth = env_int("PAB200_DEPTH", 2);
   if (depth < 2 || depth > pab::kMaxDepth)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_DEPTH must be in [2, %d]", pab::kMaxDepth);
-  int warps_per_sm = static_cast<int>((200u * 1024u) / (depth * stage));
-  if (warps_per_sm < 1) warps_per_sm = 1;
-  int wpc = warps_per_sm;
-  while (wpc > pab::kMaxWarpsPerCta) wpc = (wpc + 1) / 2;
-  wpc = env_int("PAB200_WPC", wpc);
-  if (wpc < 1 || wpc > pab::kMaxWarpsPerCta)
-    return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_WPC must be in [1, %d]", pab::kMaxWarpsPerCta);
+  Geometry geo;
+  if ((rc = choose_geometry(pl->ops, dev, depth, stage, pl->nt, env_int("PAB200_WPC", 0), &geo)))
+    return rc;
+  const int wpc = geo.wpc, per_sm = geo.per_sm;
   pl->depth = depth;
   pl->wpc = wpc;
-  pl->smem = 1024 + size_t(wpc) * depth * stage +
-             size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + 2 * pl->nt * 8 * 4);
-  if (pl->smem > 232448)
-    return fail(PAB200_ERR_UNSUPPORTED, "shared memory %zu exceeds 227 KiB", pl->smem);
-
-  e = cudaFuncSetAttribute(pl->ops.fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(pl->smem));
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pl->ops.fn, wpc * 32, pl->smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-  if (per_sm < 1) return fail(PAB200_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
+  pl->smem = geo.smem;
   pl->ctas_per_sm = per_sm;
   int W = sms * per_sm * wpc;
   pl->n_heads = a->num_seqs * a->num_kv_heads;
@@ -246,6 +304,15 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   }
   pl->W = W;
   pl->grid = (W + wpc - 1) / wpc;
+  // Split heads are merged either by their last warp inside the decode kernel
+  // (one warp per head, on the kernel's tail) or by reduce_kernel (one warp
+  // per output row).  The tail merge wins while a head's partials are few
+  // and small; estimate its bytes with every head of equal length.
+  {
+    const double spans = double(W) / pl->n_heads + 1.0;
+    const double merge_bytes = spans * pl->G * D * 4.0;
+    pl->merge_in_kernel = env_int("PAB200_MERGE", merge_bytes > 16384.0 ? 1 : 0) ? 1 : 0;
+  }
 
   pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
   size_t off = 256;  // status word
@@ -284,6 +351,12 @@ int encode_cache_map(const pab200_decode_args* a, const void* base, CUtensorMap*
 template <typename T>
 cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s) {
   pab::plan_kernel<T><<<1, 1024, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_reduce(const pab::DecodeParams& p, int rows, cudaStream_t s) {
+  pab::reduce_kernel<T><<<(rows + 7) / 8, 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -343,6 +416,7 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   p.slot_floats = pl.slot_floats;
   p.state_o = a->state_o;
   p.state_lse = a->state_lse;
+  p.merge_in_kernel = pl.merge_in_kernel;
 
   CUtensorMap kmap, vmap;
   if (a->num_pages > 0) {
@@ -367,6 +441,12 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   if (a->event_after) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_after), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  if (pl.merge_in_kernel) {
+    const int rows = pl.n_heads * pl.G;
+    e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, rows, s)
+                                      : launch_reduce<__half>(p, rows, s);
+    if (e != cudaSuccess) return cuda_fail(e, "reduce kernel launch");
   }
   return PAB200_OK;
 }

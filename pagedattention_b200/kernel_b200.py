@@ -64,17 +64,29 @@ def _as_int32(t: torch.Tensor, name: str) -> torch.Tensor:
     raise TypeError(f"{name} must be an integer tensor, got {t.dtype}")
 
 
-def _workspace(lib, args, device, stream) -> torch.Tensor:
-    need = lib.pab200_decode_workspace_size(ctypes.byref(args))
-    if need == 0:
-        raise ValueError(f"pab200_decode_workspace_size: {lib.pab200_last_error().decode()}")
-    key = (device.index, stream.cuda_stream)
-    with _ws_lock:
-        ws = _workspaces.get(key)
-        if ws is None or ws.numel() < need:
-            ws = torch.empty(need, dtype=torch.uint8, device=device)
-            _workspaces[key] = ws
-        _last_ws[device.index] = (ws, stream.cuda_stream)
+_ws_sizes: dict[tuple, int] = {}
+
+
+def _workspace(lib, args, device, stream_handle) -> torch.Tensor:
+    # The size depends only on shapes and the device, so it is cached per
+    # shape key (the C call re-plans the launch geometry).
+    skey = (device.index, args.num_seqs, args.num_q_heads, args.num_kv_heads, args.head_size,
+            args.block_size, args.dtype, args.num_splits, args.max_blocks)
+    need = _ws_sizes.get(skey)
+    if need is None:
+        need = lib.pab200_decode_workspace_size(ctypes.byref(args))
+        if need == 0:
+            raise ValueError(f"pab200_decode_workspace_size: {lib.pab200_last_error().decode()}")
+        _ws_sizes[skey] = need
+    key = (device.index, stream_handle)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        with _ws_lock:
+            ws = _workspaces.get(key)
+            if ws is None or ws.numel() < need:
+                ws = torch.empty(need, dtype=torch.uint8, device=device)
+                _workspaces[key] = ws
+    _last_ws[device.index] = (ws, stream_handle)
     return ws
 
 
@@ -97,14 +109,26 @@ def _run_decode(args: _lib.DecodeArgs, device: torch.device) -> None:
     if ev is not None:
         args.event_before = ev[0].cuda_event
         args.event_after = ev[1].cuda_event
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device)
-        ws = _workspace(lib, args, device, stream)
-        rc = lib.pab200_decode(ctypes.byref(args), ctypes.c_void_p(ws.data_ptr()),
-                               ws.numel(), ctypes.c_void_p(stream.cuda_stream))
+    if torch.cuda.current_device() == device.index:
+        rc = _launch(lib, args, device)
+    else:
+        with torch.cuda.device(device):
+            rc = _launch(lib, args, device)
     if rc == _lib.ERR_INVALID_ARGUMENT or rc == _lib.ERR_UNSUPPORTED:
         raise ValueError(f"pab200_decode: {_lib.error_text(lib, rc)}")
     _lib.check(lib, rc, "pab200_decode")
+
+
+def _launch(lib, args, device) -> int:
+    stream_handle = torch.cuda.current_stream(device).cuda_stream
+    ws = _workspace(lib, args, device, stream_handle)
+    rc = lib.pab200_decode(ctypes.byref(args), ws.data_ptr(), ws.numel(), stream_handle)
+    if rc == _lib.ERR_WORKSPACE:
+        # launch geometry changed (e.g. a tuning variable): re-size once
+        _ws_sizes.clear()
+        ws = _workspace(lib, args, device, stream_handle)
+        rc = lib.pab200_decode(ctypes.byref(args), ws.data_ptr(), ws.numel(), stream_handle)
+    return rc
 
 
 def _fill_common(args, *, q, k_cache, v_cache, lens, bt, dtype, B, Hq, Hkv, D, bs,

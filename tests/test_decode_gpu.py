@@ -90,3 +90,18 @@ def test_known_answers(cuda_device):
     for g in range(4):
         assert torch.equal(out[0, 0, g], v[page, 0])
     assert torch.count_nonzero(out[0, 0, 4:]) == 0
+
+
+@pytest.mark.parametrize("mode", ["0", "1"])
+@pytest.mark.parametrize("B,Hkv,G,D,bs,dtype", [(3, 2, 4, 128, 16, torch.bfloat16),
+                                                 (2, 1, 32, 64, 8, torch.float16),
+                                                 (2, 2, 1, 256, 32, torch.bfloat16)])
+def test_merge_modes_agree(cuda_device, monkeypatch, mode, B, Hkv, G, D, bs, dtype):
+    """Split heads merged by their last warp (PAB200_MERGE=0) or by the
+    separate reduce kernel (PAB200_MERGE=1) give the oracle's result."""
+    monkeypatch.setenv("PAB200_MERGE", mode)
+    lens = [[3000 - 700 * h - 300 * s for h in range(Hkv)] for s in range(B)]
+    q, k, v, sl, bt, scale = random_case(B, Hkv, G, D, bs, lens, dtype, seed=31)
+    dev = cuda_device
+    out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
+    assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"merge mode {mode}")
