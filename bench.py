@@ -236,7 +236,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode
-    from pagedattention_b200.kernel_b200 import kernel_events
+    from pagedattention_b200.kernel_b200 import kernel_events, launches_per_call
     from pagedattention_b200.workloads import WORKLOADS, make_inputs
 
     rank, world, local = dist_env()
@@ -263,21 +263,32 @@ def run_b200(args):
     bt = bt.contiguous()
     kv_bytes = inp.kv_bytes()
     L2 = torch.cuda.get_device_properties(dev).L2_cache_size
-    if kv_bytes <= 3 * L2:
-        raise SystemExit("workload KV fits in L2; this bench relies on inputs larger than L2")
+    # Keep every step's KV out of L2: workloads whose KV is under 3x L2
+    # rotate over enough independent copies of the cache (same block table)
+    # that the KV read by consecutive steps together exceeds 3x L2.
+    pool_bytes = k.numel() * k.element_size() * 2
+    copies = max(1, -(-3 * L2 // kv_bytes)) if kv_bytes <= 3 * L2 else 1
+    caches = [(k, v)] + [(k.clone(), v.clone()) for _ in range(copies - 1)]
+    if copies == 1:
+        l2_note = (f"inputs larger than L2 ({kv_bytes / 2**20:.0f} MiB KV per step vs "
+                   f"{L2 / 2**20:.0f} MiB L2), no flush")
+    else:
+        l2_note = (f"{kv_bytes / 2**20:.0f} MiB KV per step < 3x L2 ({L2 / 2**20:.0f} MiB): steps "
+                   f"rotate over {copies} copies of the cache ({copies * kv_bytes / 2**20:.0f} MiB "
+                   f"of KV read per rotation)")
+    step_no = [0]
 
     def step():
-        return decode(q, k, v, sl, bt, inp.scale)
+        kc, vc = caches[step_no[0] % copies]
+        step_no[0] += 1
+        return decode(q, kc, vc, sl, bt, inp.scale)
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
 
     K = args.steps
-    kb = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    ka = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    for e in kb + ka:
-        e.record()  # create the events before the timed region
+    launches = launches_per_call(q, k, v, sl, bt, inp.scale)
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     barrier()
@@ -285,18 +296,34 @@ def run_b200(args):
     sampler = ClockSampler(dev)
     with sampler:
         t_start.record()
-        for i in range(K):
-            with kernel_events(kb[i], ka[i]):
-                step()
+        for _ in range(K):
+            step()
         t_end.record()
         torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
-    kernel_ms = statistics.fmean(b.elapsed_time(a) for b, a in zip(kb, ka))
-    kernel_ms = max_over_ranks(kernel_ms)
     ms_per_step = elapsed_ms / K
     value = kv_bytes * world * K / (elapsed_ms / 1e3) / 1e9
+
+    # Kernel-only timing for the roofline: the same K steps again, with the
+    # library recording an event pair around every decode-kernel launch on
+    # the launching stream.  (A separate pass, because recording events
+    # between the planner and decode launches disables their overlap.)
+    kb = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ka = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for e in kb + ka:
+        e.record()  # create the events before the timed pass
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        with kernel_events(kb[i], ka[i]):
+            step()
+    torch.cuda.synchronize()
+    barrier()
+    kernel_ms = statistics.fmean(b.elapsed_time(a) for b, a in zip(kb, ka))
+    kernel_ms = max_over_ranks(kernel_ms)
 
     # e2e: per-step inputs from pinned host memory, output read back.
     q_h = q.cpu().pin_memory()
@@ -309,7 +336,9 @@ def run_b200(args):
         q_d.copy_(q_h, non_blocking=True)
         sl_d.copy_(sl_h, non_blocking=True)
         bt_d.copy_(bt_h, non_blocking=True)
-        out = decode(q_d, k, v, sl_d, bt_d, inp.scale)
+        kc, vc = caches[step_no[0] % copies]
+        step_no[0] += 1
+        out = decode(q_d, kc, vc, sl_d, bt_d, inp.scale)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(3):
@@ -350,8 +379,7 @@ def run_b200(args):
                        "num_kv_heads": w.num_kv_heads, "head_size": w.head_size,
                        "block_size": w.block_size, "kv_bytes_per_gpu_step": kv_bytes,
                        "parallelism": f"dp{world} (independent sequence batches, no collective)",
-                       "l2": f"inputs larger than L2 ({kv_bytes / 2**20:.0f} MiB KV per step "
-                             f"vs {L2 / 2**20:.0f} MiB L2), no flush"},
+                       "l2": l2_note},
             "us_per_call": round(ms_per_step * 1e3, 2),
             "hbm_frac_of_measured_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -366,7 +394,7 @@ def run_b200(args):
                     "note": "public wrapper; q, cache_seqlens, block_table H2D from pinned "
                             "memory and the output D2H every step; KV cache resident"},
             "clocks": sampler.summary(),
-            "gpu_launches": 2 * K,
+            "gpu_launches": launches * K,
         }
     if world > 1:
         barrier()

@@ -42,6 +42,7 @@ STATUS_WAIT_TIMEOUT = 0x8
 
 EXPORTED_SYMBOLS = (
     "pab200_decode_workspace_size",
+    "pab200_decode_launch_count",
     "pab200_decode",
     "pab200_decode_noalloc",
     "pab200_paged_attention",
@@ -112,6 +113,8 @@ def load() -> ctypes.CDLL:
     P = ctypes.POINTER(DecodeArgs)
     lib.pab200_decode_workspace_size.argtypes = [P]
     lib.pab200_decode_workspace_size.restype = ctypes.c_size_t
+    lib.pab200_decode_launch_count.argtypes = [P]
+    lib.pab200_decode_launch_count.restype = ctypes.c_int
     lib.pab200_decode.argtypes = [P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     # plain Python ints are accepted for the pointer and size arguments
     lib.pab200_decode.restype = ctypes.c_int

@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   const int n_heads = p.B * p.Hkv;
   const int cap = p.maxb * p.bs;
   const int Hq = p.Hkv * p.G;
+  grid_launch_dependents();  // the decode grid may start its prologue now
   if (tid == 0) {
     carry = 0;
     *p.status = 0u;
@@ -282,6 +283,8 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int wpc = blockDim.x >> 5;
   const int depth = p.depth;
   const int gw = blockIdx.x * wpc + warp;
+  // Everything below reads what the planner wrote.
+  grid_dependency_wait();
   const int W = *p.weff;  // min(total_warps, total pages), set by the planner
   if (gw >= W) return;
 
@@ -819,6 +822,7 @@ __global__ void __launch_bounds__(256) reduce_kernel(const DecodeParams p) {
   const int G = p.G, D = p.D;
   const int n_heads = p.B * p.Hkv;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);  // hd * G + g
+  grid_dependency_wait();  // partials written by the decode grid
   if (row >= n_heads * G) return;
   const int hd = row / G, g = row - hd * G;
   const int c0 = p.cum[hd], c1 = p.cum[hd + 1];
@@ -866,15 +870,15 @@ __global__ void __launch_bounds__(256) reduce_kernel(const DecodeParams p) {
     const bool active = c < D;
     const int cc = active ? c : 0;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j0 = 0; j0 < nspans; j0 += 8) {
-      float4 v[8];
+    for (int j0 = 0; j0 < nspans; j0 += 16) {
+      float4 v[16];
 #pragma unroll
-      for (int b = 0; b < 8; ++b) {
+      for (int b = 0; b < 16; ++b) {
         const int j = j0 + b < nspans ? j0 + b : nspans - 1;
         v[b] = __ldcg(reinterpret_cast<const float4*>(base + static_cast<int64_t>(j) * sf + g * D + cc));
       }
 #pragma unroll
-      for (int b = 0; b < 8; ++b) {
+      for (int b = 0; b < 16; ++b) {
         const int j = j0 + b;
         const int r = (j >> 5) & 3;  // warp-uniform
         const float src = r == 0 ? wj[0] : (r == 1 ? wj[1] : (r == 2 ? wj[2] : wj[3]));

@@ -4,8 +4,9 @@
 // (src/kernel_triton.py:181-307).  Differences by design: the chunk plan is
 // computed on the device (no .cpu() sync, no per-call H2D metadata copies,
 // src/kernel_triton.py:206-229), the partial buffers live in a caller-owned
-// workspace (no per-call allocation, :232-243), and the split and reduce
-// kernels are one launch.
+// workspace (no per-call allocation, :232-243), and split heads are merged
+// inside the split kernel unless their partial states are large, in which
+// case a separate reduce kernel (the reference's own structure) runs.
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -74,16 +75,34 @@ int env_int(const char* name, int fallback) {
 // ------------------------------------------------------------------ kernels
 struct KernelOps {
   void* fn;  // decode kernel (for attributes / occupancy)
-  cudaError_t (*launch)(dim3, dim3, size_t, cudaStream_t, const CUtensorMap&,
+  cudaError_t (*launch)(dim3, dim3, size_t, cudaStream_t, bool, const CUtensorMap&,
                         const CUtensorMap&, const pab::DecodeParams&);
 };
 
+// Launch configuration; `pdl` lets the grid start while the previous kernel
+// in the stream finishes (programmatic dependent launch): the kernel waits
+// with griddepcontrol.wait before it reads that kernel's output.
+struct LaunchCfg {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  LaunchCfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl) {
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+  }
+};
+
 template <typename T, int D, int NT, int ST>
-cudaError_t launch_decode(dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+cudaError_t launch_decode(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
                           const CUtensorMap& k, const CUtensorMap& v,
                           const pab::DecodeParams& p) {
-  pab::decode_kernel<T, D, NT, ST><<<grid, block, smem, s>>>(k, v, p);
-  return cudaGetLastError();
+  LaunchCfg lc(grid, block, smem, s, pdl);
+  return cudaLaunchKernelEx(&lc.cfg, pab::decode_kernel<T, D, NT, ST>, k, v, p);
 }
 
 template <typename T, int D, int NT, int ST>
@@ -355,9 +374,9 @@ cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s) {
 }
 
 template <typename T>
-cudaError_t launch_reduce(const pab::DecodeParams& p, int rows, cudaStream_t s) {
-  pab::reduce_kernel<T><<<(rows + 7) / 8, 256, 0, s>>>(p);
-  return cudaGetLastError();
+cudaError_t launch_reduce(const pab::DecodeParams& p, int rows, cudaStream_t s, bool pdl) {
+  LaunchCfg lc(dim3((rows + 7) / 8), dim3(256), 0, s, pdl);
+  return cudaLaunchKernelEx(&lc.cfg, pab::reduce_kernel<T>, p);
 }
 
 }  // namespace
@@ -366,6 +385,12 @@ PAB200_EXPORT size_t pab200_decode_workspace_size(const pab200_decode_args* args
   Plan pl;
   if (make_plan(args, &pl) != PAB200_OK) return 0;
   return pl.ws_bytes;
+}
+
+PAB200_EXPORT int pab200_decode_launch_count(const pab200_decode_args* args) {
+  Plan pl;
+  if (make_plan(args, &pl) != PAB200_OK) return 0;
+  return pl.merge_in_kernel ? 3 : 2;
 }
 
 PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
@@ -436,7 +461,9 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
     e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_before), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  e = pl.ops.launch(dim3(pl.grid), dim3(pl.wpc * 32), pl.smem, s, kmap, vmap, p);
+  const bool pdl = env_int("PAB200_PDL", 1) != 0;
+  e = pl.ops.launch(dim3(pl.grid), dim3(pl.wpc * 32), pl.smem, s, pdl && !a->event_before, kmap,
+                    vmap, p);
   if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
   if (a->event_after) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_after), s);
@@ -444,8 +471,9 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   }
   if (pl.merge_in_kernel) {
     const int rows = pl.n_heads * pl.G;
-    e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, rows, s)
-                                      : launch_reduce<__half>(p, rows, s);
+    const bool pdl_r = pdl && !a->event_after;
+    e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, rows, s, pdl_r)
+                                      : launch_reduce<__half>(p, rows, s, pdl_r);
     if (e != cudaSuccess) return cuda_fail(e, "reduce kernel launch");
   }
   return PAB200_OK;

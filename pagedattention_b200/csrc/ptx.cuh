@@ -21,6 +21,18 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// Wait until the grids this launch depends on have completed and their memory
+// is visible (a no-op for a launch without a programmatic dependency).
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Let the dependent launch start being scheduled before this grid ends.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count)

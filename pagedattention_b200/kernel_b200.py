@@ -90,6 +90,31 @@ def _workspace(lib, args, device, stream_handle) -> torch.Tensor:
     return ws
 
 
+def launches_per_call(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale,
+                      num_splits=1) -> int:
+    """Kernel launches one flash_attn_with_kvcache_wrapper_b200 call with these
+    arguments makes (2, or 3 when a separate reduce kernel merges split heads)."""
+    Hq, Hkv, G, D = _validate_decode_inputs(q, cache_seqlens, block_table)
+    args = _lib.DecodeArgs()
+    lens = _as_int32(cache_seqlens, "cache_seqlens")
+    bt = _as_int32(block_table, "block_table")
+    _fill_common(args, q=q, k_cache=k_cache, v_cache=v_cache, lens=lens, bt=bt, dtype=q.dtype,
+                 B=q.shape[0], Hq=Hq, Hkv=Hkv, D=D, bs=k_cache.shape[1],
+                 num_pages=k_cache.shape[0], scale=softmax_scale, num_splits=num_splits)
+    args.out, args.layout, args.max_blocks = q.data_ptr(), _lib.LAYOUT_PAGES, bt.shape[2]
+    args.q_stride_b, args.q_stride_h = q.stride(0), q.stride(2)
+    args.out_stride_b, args.out_stride_h = q.stride(0), q.stride(2)
+    args.seqlens_stride_b, args.seqlens_stride_h = lens.stride(0), lens.stride(1)
+    args.bt_stride_b, args.bt_stride_h, args.bt_stride_i = bt.stride(0), bt.stride(1), bt.stride(2)
+    args.bt_page_mul = 1
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        n = lib.pab200_decode_launch_count(ctypes.byref(args))
+    if n == 0:
+        raise ValueError(f"pab200_decode_launch_count: {lib.pab200_last_error().decode()}")
+    return n
+
+
 @contextmanager
 def kernel_events(before: torch.cuda.Event, after: torch.cuda.Event):
     """Record ``before``/``after`` around the main decode kernel of every
