@@ -49,6 +49,12 @@ constexpr uint32_t kStatusClamp = 0x2u;
 constexpr uint32_t kStatusNegative = 0x4u;
 constexpr uint32_t kStatusTimeout = 0x8u;
 constexpr int kMetaBytesPerSlot = 32;  // two int4 per ring slot
+constexpr int kCoreMaxG = 4;           // largest query group of the CUDA-core path
+
+// Per-warp shared memory of the CUDA-core path: the query group in fp32.
+__host__ __device__ constexpr int core_q_bytes(bool core, int D) {
+  return core ? kCoreMaxG * D * 4 : 0;
+}
 
 struct DecodeParams {
   void* out;
@@ -253,10 +259,62 @@ __device__ __forceinline__ void merge_accumulate(const float* base, int sf, int 
 }
 
 // --------------------------------------------------------------------------
+// Shared-memory helpers of the CUDA-core path.
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+// Eight 16-bit values (one 16-byte chunk) to fp32.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]);
+template <>
+__device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // bf16 -> fp32 is a 16-bit left shift
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void unpack8<__half>(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// DL consecutive 16-bit values at shared address `addr` to fp32 (DL = 2 or 4).
+template <typename T, int DL>
+__device__ __forceinline__ void load_row_part(uint32_t addr, float (&f)[DL]) {
+  float t[8];
+  if constexpr (DL == 4) {
+    uint32_t a, b;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
+    unpack8<T>(make_uint4(a, b, 0u, 0u), t);
+  } else {
+    uint32_t a;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a) : "r"(addr));
+    unpack8<T>(make_uint4(a, 0u, 0u, 0u), t);
+  }
+#pragma unroll
+  for (int i = 0; i < DL; ++i) f[i] = t[i];
+}
+
+// --------------------------------------------------------------------------
 // Decode kernel.  T: element type; D: head size; NT: query-head tiles of 8
 // (G <= 8*NT); ST: tokens per ring stage (16, 32 or 64; a power of two
-// >= block_size).
-template <typename T, int D, int NT, int ST>
+// >= block_size).  CORE selects CUDA-core arithmetic instead of tensor-core
+// MMA for small query groups (G <= kCoreMaxG, ST == 32): one token per lane
+// for q.K, a warp-shuffle softmax, lanes over the head dimension for P.V.
+template <typename T, int D, int NT, int ST, bool CORE>
 __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     decode_kernel(const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap,
@@ -271,6 +329,8 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   constexpr int STAGE_BYTES = 2 * KV_BYTES;
   constexpr int GP = NT * 8;  // padded query-group size
   static_assert(D % 64 == 0 && (ST == 16 || ST == 32 || ST == 64), "shape");
+  static_assert(!CORE || (ST == 32 && NT == 1 && D <= 128), "CUDA-core path shape");
+  constexpr int DL = D / 32;  // head-dim elements per lane (CUDA-core path)
   static_assert(NH == 1 || NH == 2 || NH == 4, "head size");
 
   extern __shared__ uint8_t smem_raw[];
@@ -309,6 +369,9 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   float* scratch = reinterpret_cast<float*>(
                        tail + wpc * kMaxDepth * (8 + kMetaBytesPerSlot)) +
                    warp * 2 * GP;
+  float* qsm = reinterpret_cast<float*>(tail + wpc * kMaxDepth * (8 + kMetaBytesPerSlot) +
+                                        wpc * 2 * GP * 4) +
+               warp * (core_q_bytes(CORE, D) / 4);
 
   if (lane == 0) {
     for (int i = 0; i < depth; ++i) mbar_init(bars + i * 8, 1);
@@ -428,10 +491,31 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   uint32_t qb[KS][NT][2];
   float acc[KS][NT][4];
   float mrun[NT][2], lrun[NT][2];
+  // CUDA-core path: lane owns head-dim elements [lane*DL, lane*DL + DL) of
+  // every query head; cm is the running max (log2 units, warp-uniform), cl
+  // this lane's part of the running sum.
+  float cacc[kCoreMaxG][DL];
+  float cm[kCoreMaxG], cl[kCoreMaxG];
 
   auto start_head = [&](int hd) {
     const int s = hd / Hkv, h = hd - s * Hkv;
     const T* qp = static_cast<const T*>(p.q) + s * p.q_sb + static_cast<int64_t>(h) * G * p.q_sh;
+    if constexpr (CORE) {
+      __syncwarp();  // the previous head's q is no longer read
+      for (int idx = lane; idx < kCoreMaxG * D; idx += 32) {
+        const int g = idx / D, d = idx - g * D;
+        qsm[idx] = g < G ? static_cast<float>(qp[g * p.q_sh + d]) : 0.f;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int g = 0; g < kCoreMaxG; ++g) {
+        cm[g] = -INFINITY;
+        cl[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DL; ++e) cacc[g][e] = 0.f;
+      }
+      return;
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int g = nt * 8 + lr;
@@ -548,6 +632,51 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   };
 
   auto finish_head = [&](int hd, int nspans, int wfirst) {
+    if constexpr (CORE) {
+      const int s = hd / Hkv, h = hd - s * Hkv;
+      const int Hq = Hkv * G;
+      float lt[kCoreMaxG];
+#pragma unroll
+      for (int g = 0; g < kCoreMaxG; ++g) {
+        float l = cl[g];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        lt[g] = l;
+      }
+      const int d0 = lane * DL;
+      if (nspans == 1) {
+#pragma unroll
+        for (int g = 0; g < kCoreMaxG; ++g) {
+          if (g >= G) break;
+          const float inv = 1.f / lt[g];
+          const int qh = h * G + g;
+          if (p.state_o) {
+            float* o = p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + d0;
+#pragma unroll
+            for (int e = 0; e < DL; ++e) o[e] = cacc[g][e] * inv;
+            if (lane == 0)
+              p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (cm[g] + __log2f(lt[g])) * kLn2;
+          } else {
+            T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + d0;
+#pragma unroll
+            for (int e = 0; e < DL; e += 2)
+              *reinterpret_cast<uint32_t*>(o + e) = pack2<T>(cacc[g][e] * inv, cacc[g][e + 1] * inv);
+          }
+        }
+        return;
+      }
+      float* ps = p.part + static_cast<int64_t>(hd + gw) * p.slot_floats;
+#pragma unroll
+      for (int g = 0; g < kCoreMaxG; ++g) {
+        if (g >= G) break;
+#pragma unroll
+        for (int e = 0; e < DL; ++e) __stcg(ps + g * D + d0 + e, cacc[g][e]);
+        if (lane == 0) {
+          __stcg(ps + G * D + g, cm[g]);
+          __stcg(ps + G * D + G + g, lt[g]);
+        }
+      }
+    } else {
     float lt[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -621,6 +750,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
           }
         }
     }
+    }  // CORE / MMA partial publication
     if (p.merge_in_kernel) return;  // reduce_kernel merges after this kernel
     __threadfence();
     __syncwarp();
@@ -667,7 +797,73 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     const int mtv = (ntok + 15) >> 4;
     const uint32_t kbase = ring + slot * STAGE_BYTES;
     const uint32_t vbase = kbase + KV_BYTES;
-
+    bool dirty = false;
+    if constexpr (CORE) {
+      // q.K on CUDA cores: lane t scores token t against every query head.
+      float sc[kCoreMaxG];
+#pragma unroll
+      for (int g = 0; g < kCoreMaxG; ++g) sc[g] = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < D / 8; ++ch) {
+        const uint4 kv = ld_shared_v4(kbase + (ch >> 3) * PLANE + lane * 128 +
+                                      static_cast<uint32_t>(((ch & 7) ^ x7) << 4));
+        float kf[8];
+        unpack8<T>(kv, kf);
+#pragma unroll
+        for (int g = 0; g < kCoreMaxG; ++g) {
+          if (g >= G) break;
+          const float4 qa = *reinterpret_cast<const float4*>(qsm + g * D + ch * 8);
+          const float4 qc = *reinterpret_cast<const float4*>(qsm + g * D + ch * 8 + 4);
+          sc[g] = fmaf(qa.x, kf[0], sc[g]);
+          sc[g] = fmaf(qa.y, kf[1], sc[g]);
+          sc[g] = fmaf(qa.z, kf[2], sc[g]);
+          sc[g] = fmaf(qa.w, kf[3], sc[g]);
+          sc[g] = fmaf(qc.x, kf[4], sc[g]);
+          sc[g] = fmaf(qc.y, kf[5], sc[g]);
+          sc[g] = fmaf(qc.z, kf[6], sc[g]);
+          sc[g] = fmaf(qc.w, kf[7], sc[g]);
+        }
+      }
+      // Online softmax across the warp (tokens are lanes); rows past the
+      // valid range are masked by selection, so stale shared memory never
+      // reaches an arithmetic result.
+      float pr[kCoreMaxG];
+#pragma unroll
+      for (int g = 0; g < kCoreMaxG; ++g) {
+        if (g >= G) break;
+        const float t = lane < ntok ? sc[g] * scale_log2 : -INFINITY;
+        float mx = t;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mnew = fmaxf(cm[g], mx);
+        const float alpha = fast_exp2(cm[g] - mnew);
+        cm[g] = mnew;
+        pr[g] = fast_exp2(t - mnew);
+        cl[g] = cl[g] * alpha + pr[g];
+        if (alpha != 1.f) {  // warp-uniform: the running max grew
+#pragma unroll
+          for (int e = 0; e < DL; ++e) cacc[g][e] *= alpha;
+        }
+      }
+      // P.V: lane owns DL consecutive head-dim elements; p of token tt comes
+      // from lane tt.  Only the ntok valid rows are read.
+      const int hf = (lane * DL) >> 6;
+      const int cidx = ((lane * DL) & 63) >> 3;
+      const uint32_t boff = static_cast<uint32_t>(((lane * DL) & 7) * 2);
+      for (int tt = 0; tt < ntok; ++tt) {
+        const uint32_t addr = vbase + hf * PLANE + tt * 128 +
+                              static_cast<uint32_t>((cidx ^ (tt & 7)) << 4) + boff;
+        float vf[DL];
+        load_row_part<T, DL>(addr, vf);
+#pragma unroll
+        for (int g = 0; g < kCoreMaxG; ++g) {
+          if (g >= G) break;
+          const float pt = __shfl_sync(0xffffffffu, pr[g], tt);
+#pragma unroll
+          for (int e = 0; e < DL; ++e) cacc[g][e] = fmaf(pt, vf[e], cacc[g][e]);
+        }
+      }
+    } else {
     // S^T = K Q^T for the valid 16-token tiles; even and odd k-steps go to
     // separate accumulators so the two MMA dependency chains overlap.
     float sc[MT][NT][4];
@@ -774,7 +970,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       }
     // V rows past the valid range may hold stale or non-finite data; zero
     // them so 0 * V stays 0.  (Whole 128-byte rows: swizzle-invariant.)
-    const bool dirty = ntok < mtv * 16;
+    dirty = ntok < mtv * 16;
     if (dirty) {
       const int nrows = mtv * 16 - ntok;
       uint4* vz = reinterpret_cast<uint4*>(smem + (vbase - smem_base));
@@ -799,6 +995,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
           for (int nt = 0; nt < NT; ++nt) mma_16816<T>(acc[dt][nt], a, pb[mt][nt][0], pb[mt][nt][1]);
         }
       }
+    }  // MMA path
     __syncwarp();
     if (dirty) {
       fence_proxy_async_smem();

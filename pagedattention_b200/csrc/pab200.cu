@@ -97,22 +97,30 @@ struct LaunchCfg {
   }
 };
 
-template <typename T, int D, int NT, int ST>
+template <typename T, int D, int NT, int ST, bool CORE>
 cudaError_t launch_decode(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
                           const CUtensorMap& k, const CUtensorMap& v,
                           const pab::DecodeParams& p) {
   LaunchCfg lc(grid, block, smem, s, pdl);
-  return cudaLaunchKernelEx(&lc.cfg, pab::decode_kernel<T, D, NT, ST>, k, v, p);
+  return cudaLaunchKernelEx(&lc.cfg, pab::decode_kernel<T, D, NT, ST, CORE>, k, v, p);
 }
 
-template <typename T, int D, int NT, int ST>
+template <typename T, int D, int NT, int ST, bool CORE = false>
 KernelOps ops_of() {
-  return KernelOps{reinterpret_cast<void*>(&pab::decode_kernel<T, D, NT, ST>),
-                   &launch_decode<T, D, NT, ST>};
+  return KernelOps{reinterpret_cast<void*>(&pab::decode_kernel<T, D, NT, ST, CORE>),
+                   &launch_decode<T, D, NT, ST, CORE>};
 }
 
 template <typename T, int ST>
-bool select_dnt(int D, int nt, KernelOps* o) {
+bool select_dnt(int D, int nt, bool core, KernelOps* o) {
+  if (core) {  // CUDA-core path: G <= 4, 32-token stages, D <= 128
+    if (ST != 32 || nt != 1) return false;
+    switch (D) {
+      case 64: *o = ops_of<T, 64, 1, 32, true>(); return true;
+      case 128: *o = ops_of<T, 128, 1, 32, true>(); return true;
+      default: return false;
+    }
+  }
   switch (D * 16 + nt) {
     case 64 * 16 + 1: *o = ops_of<T, 64, 1, ST>(); return true;
     case 64 * 16 + 2: *o = ops_of<T, 64, 2, ST>(); return true;
@@ -124,19 +132,19 @@ bool select_dnt(int D, int nt, KernelOps* o) {
   }
 }
 
-bool select_kernel(int dtype, int D, int nt, int st, KernelOps* o) {
+bool select_kernel(int dtype, int D, int nt, int st, bool core, KernelOps* o) {
   if (dtype == PAB200_DTYPE_BF16) {
     switch (st) {
-      case 16: return select_dnt<__nv_bfloat16, 16>(D, nt, o);
-      case 32: return select_dnt<__nv_bfloat16, 32>(D, nt, o);
-      case 64: return select_dnt<__nv_bfloat16, 64>(D, nt, o);
+      case 16: return select_dnt<__nv_bfloat16, 16>(D, nt, core, o);
+      case 32: return select_dnt<__nv_bfloat16, 32>(D, nt, core, o);
+      case 64: return select_dnt<__nv_bfloat16, 64>(D, nt, core, o);
       default: return false;
     }
   }
   switch (st) {
-    case 16: return select_dnt<__half, 16>(D, nt, o);
-    case 32: return select_dnt<__half, 32>(D, nt, o);
-    case 64: return select_dnt<__half, 64>(D, nt, o);
+    case 16: return select_dnt<__half, 16>(D, nt, core, o);
+    case 32: return select_dnt<__half, 32>(D, nt, core, o);
+    case 64: return select_dnt<__half, 64>(D, nt, core, o);
     default: return false;
   }
 }
@@ -146,6 +154,7 @@ struct Plan {
   KernelOps ops;
   int G, nt, st, wpc, depth, ctas_per_sm, grid, W;
   int merge_in_kernel;
+  bool core;
   size_t smem;
   int n_heads;
   int slot_floats;
@@ -208,9 +217,9 @@ int validate(const pab200_decode_args* a) {
 
 // Dynamic shared memory of one decode CTA: ring slots, then per-warp
 // mbarriers, stage records and merge scratch (see decode_kernel).
-size_t decode_smem(int wpc, int depth, size_t stage, int nt) {
+size_t decode_smem(int wpc, int depth, size_t stage, int nt, int core_bytes) {
   return 1024 + size_t(wpc) * depth * stage +
-         size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + 2 * nt * 8 * 4);
+         size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + 2 * nt * 8 * 4 + core_bytes);
 }
 
 struct Geometry {
@@ -223,8 +232,8 @@ struct Geometry {
 // try every CTA size and keep the one with the most warps per SM (shared
 // memory and registers both limit it; ties go to the larger CTA).  Results
 // are cached per device, kernel, ring depth and stage size.
-int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, int nt, int forced_wpc,
-                    Geometry* out) {
+int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, int nt, int core_bytes,
+                    int forced_wpc, Geometry* out) {
   struct Entry {
     int dev;
     void* fn;
@@ -264,7 +273,7 @@ int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, int 
   Geometry best{0, 0, 0};
   for (int ci = 0; ci < ncand; ++ci) {
     const int wpc = cand[ci];
-    const size_t smem = decode_smem(wpc, depth, stage, nt);
+    const size_t smem = decode_smem(wpc, depth, stage, nt, core_bytes);
     if (smem > 232448) continue;
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops.fn, wpc * 32, smem);
@@ -296,7 +305,11 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   const int nh = D / 64;
   if (2 * (pl->st / bs) * nh > 32)
     return fail(PAB200_ERR_UNSUPPORTED, "block_size %d with head_size %d needs > 32 copies per stage", bs, D);
-  if (!select_kernel(a->dtype, D, pl->nt, pl->st, &pl->ops))
+  // Arithmetic: tensor-core MMA by default; the CUDA-core variant
+  // (PAB200_CORE=1) exists for query groups of at most 4 heads, 32-token
+  // stages and D <= 128.
+  pl->core = env_int("PAB200_CORE", 0) != 0 && pl->G <= pab::kCoreMaxG && pl->st == 32 && D <= 128;
+  if (!select_kernel(a->dtype, D, pl->nt, pl->st, pl->core, &pl->ops))
     return fail(PAB200_ERR_UNSUPPORTED, "no kernel for head_size %d, group %d", D, pl->G);
 
   // Each warp owns a private ring of `depth` stages.  Throughput grows with
@@ -308,7 +321,8 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   if (depth < 2 || depth > pab::kMaxDepth)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_DEPTH must be in [2, %d]", pab::kMaxDepth);
   Geometry geo;
-  if ((rc = choose_geometry(pl->ops, dev, depth, stage, pl->nt, env_int("PAB200_WPC", 0), &geo)))
+  if ((rc = choose_geometry(pl->ops, dev, depth, stage, pl->nt, pab::core_q_bytes(pl->core, D),
+                            env_int("PAB200_WPC", 0), &geo)))
     return rc;
   const int wpc = geo.wpc, per_sm = geo.per_sm;
   pl->depth = depth;

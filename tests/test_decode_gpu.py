@@ -105,3 +105,21 @@ def test_merge_modes_agree(cuda_device, monkeypatch, mode, B, Hkv, G, D, bs, dty
     dev = cuda_device
     out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
     assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"merge mode {mode}")
+
+
+@pytest.mark.parametrize("merge", ["0", "1"])
+@pytest.mark.parametrize("B,Hkv,G,D,bs,dtype", [(3, 4, 1, 128, 16, torch.float16),
+                                                 (2, 2, 2, 128, 32, torch.bfloat16),
+                                                 (3, 2, 4, 128, 16, torch.bfloat16),
+                                                 (2, 3, 3, 64, 8, torch.float16)])
+def test_cuda_core_path_vs_oracle(cuda_device, monkeypatch, merge, B, Hkv, G, D, bs, dtype):
+    """The CUDA-core arithmetic variant (PAB200_CORE=1, query groups <= 4)
+    against the oracle, over lengths 0..1000 and both merge modes."""
+    monkeypatch.setenv("PAB200_CORE", "1")
+    monkeypatch.setenv("PAB200_MERGE", merge)
+    pool = [0, 1, bs - 1, bs, bs + 1, 31, 32, 33, 200, 513, 1000]
+    lens = [[pool[(s * Hkv + h * 3) % len(pool)] for h in range(Hkv)] for s in range(B)]
+    q, k, v, sl, bt, scale = random_case(B, Hkv, G, D, bs, lens, dtype, seed=G * 10 + B)
+    dev = cuda_device
+    out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
+    assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"CUDA-core G{G} D{D} bs{bs}")
