@@ -53,6 +53,12 @@ def parse_args():
                     help="wall budget of the CPU-baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--mode", choices=["replicate", "shard", "split"], default=None,
+                    help="N>1: replicate = every rank its own batch (weak scaling); shard = "
+                         "one batch's sequences split over ranks (strong); split = every "
+                         "sequence's context split over ranks, NCCL state merge (strong). "
+                         "Default: split for long_context, shard for llama70b_mixed, "
+                         "else replicate")
     return ap.parse_args()
 
 
@@ -236,8 +242,10 @@ def run_b200(args):
     import torch.distributed as dist
 
     from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode
+    from pagedattention_b200.distributed import (context_ranges, decode_context_parallel,
+                                                 shard_sequences)
     from pagedattention_b200.kernel_b200 import kernel_events, launches_per_call
-    from pagedattention_b200.workloads import WORKLOADS, make_inputs
+    from pagedattention_b200.workloads import WORKLOADS, make_inputs, sample_lens
 
     rank, world, local = dist_env()
     if world != args.gpus:
@@ -258,10 +266,31 @@ def run_b200(args):
         return float(t.item())
 
     w = WORKLOADS[args.workload]
-    inp = make_inputs(w, seed=args.seed + rank, device=dev, gen_device=dev)
+    mode = args.mode or {"long_context": "split", "llama70b_mixed": "shard"}.get(w.name,
+                                                                                 "replicate")
+    if world == 1:
+        mode = "replicate"
+    elt = 2
+    lens_all = sample_lens(w, args.seed)
+    global_bytes = int(lens_all.to(torch.int64).sum()) * w.num_kv_heads * w.head_size * elt * 2
+    if mode == "replicate":      # every rank decodes its own batch
+        inp = make_inputs(w, seed=args.seed + rank, device=dev, gen_device=dev)
+        parallelism = f"dp{world} (independent sequence batches per rank, no collective)"
+    elif mode == "shard":        # one batch, sequences split over ranks (LPT by tokens)
+        idx = shard_sequences(lens_all.tolist(), world)[rank]
+        inp = make_inputs(w, seed=args.seed + rank, device=dev, gen_device=dev,
+                          lens=lens_all[idx])
+        parallelism = f"sequence-sharded over {world} ranks (LPT by tokens), no collective"
+    else:                        # every context split over ranks, states merged over NCCL
+        starts, ends = context_ranges(lens_all, world, w.partition_tokens or 512)
+        inp = make_inputs(w, seed=args.seed, device=dev, gen_device=dev,
+                          lens=(ends[rank] - starts[rank]).to(torch.int32))
+        parallelism = (f"context split over {world} ranks ({w.partition_tokens or 512}-token "
+                       "aligned ranges), (o, lse) states all-gathered over NCCL and merged")
     q, k, v, sl, bt = inp.reference_layout()
     bt = bt.contiguous()
     kv_bytes = inp.kv_bytes()
+    total_bytes = kv_bytes * world if mode == "replicate" else global_bytes
     L2 = torch.cuda.get_device_properties(dev).L2_cache_size
     # Keep every step's KV out of L2: workloads whose KV is under 3x L2
     # rotate over enough independent copies of the cache (same block table)
@@ -278,10 +307,23 @@ def run_b200(args):
                    f"of KV read per rotation)")
     step_no = [0]
 
-    def step():
-        kc, vc = caches[step_no[0] % copies]
+    kpool_copies = [(inp.k_pool, inp.v_pool)] + [
+        (kc.view_as(inp.k_pool), vc.view_as(inp.v_pool)) for kc, vc in caches[1:]]
+
+    def run(qx, slx, btx, seq_bt, seq_lens):
+        i = step_no[0] % copies
         step_no[0] += 1
-        return decode(q, kc, vc, sl, bt, inp.scale)
+        if mode == "split":
+            kp, vp = kpool_copies[i]
+            return decode_context_parallel(qx[:, 0], kp, vp, seq_bt, seq_lens, inp.scale,
+                                           w.block_size)
+        kc, vc = caches[i]
+        return decode(qx, kc, vc, slx, btx, inp.scale)
+
+    seq_bt, seq_lens = inp.block_tables, inp.context_lens
+
+    def step():
+        return run(q, sl, bt, seq_bt, seq_lens)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -304,7 +346,7 @@ def run_b200(args):
     torch.cuda.synchronize()
     elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
     ms_per_step = elapsed_ms / K
-    value = kv_bytes * world * K / (elapsed_ms / 1e3) / 1e9
+    value = total_bytes * K / (elapsed_ms / 1e3) / 1e9
 
     # Kernel-only timing for the roofline: the same K steps again, with the
     # library recording an event pair around every decode-kernel launch on
@@ -323,22 +365,27 @@ def run_b200(args):
     torch.cuda.synchronize()
     barrier()
     kernel_ms = statistics.fmean(b.elapsed_time(a) for b, a in zip(kb, ka))
+    # per-GPU kernel throughput of the slowest rank
+    achieved = -max_over_ranks(-(kv_bytes / (kernel_ms / 1e3) / 1e9))
     kernel_ms = max_over_ranks(kernel_ms)
 
     # e2e: per-step inputs from pinned host memory, output read back.
-    q_h = q.cpu().pin_memory()
-    sl_h = sl.cpu().pin_memory()
-    bt_h = bt.cpu().pin_memory()
-    q_d, sl_d, bt_d = torch.empty_like(q), torch.empty_like(sl), torch.empty_like(bt)
-    out_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    # (split mode: the per-rank block table and lengths of its token range)
+    if mode == "split":
+        ins = [q, seq_lens, seq_bt]
+    else:
+        ins = [q, sl, bt]
+    hosts = [t.cpu().pin_memory() for t in ins]
+    devs = [torch.empty_like(t) for t in ins]
+    out_h = torch.empty(q[:, 0].shape if mode == "split" else q.shape, dtype=q.dtype).pin_memory()
 
     def e2e_step():
-        q_d.copy_(q_h, non_blocking=True)
-        sl_d.copy_(sl_h, non_blocking=True)
-        bt_d.copy_(bt_h, non_blocking=True)
-        kc, vc = caches[step_no[0] % copies]
-        step_no[0] += 1
-        out = decode(q_d, kc, vc, sl_d, bt_d, inp.scale)
+        for d, h in zip(devs, hosts):
+            d.copy_(h, non_blocking=True)
+        if mode == "split":
+            out = run(devs[0], None, None, devs[2], devs[1])
+        else:
+            out = run(devs[0], devs[1], devs[2], None, None)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(3):
@@ -354,12 +401,11 @@ def run_b200(args):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e_value = kv_bytes * world * E / (e2e_ms / 1e3) / 1e9
-    h2d = q_h.numel() * q_h.element_size() + sl_h.numel() * 4 + bt_h.numel() * 4
+    e2e_value = total_bytes * E / (e2e_ms / 1e3) / 1e9
+    h2d = sum(h.numel() * h.element_size() for h in hosts)
     d2h = out_h.numel() * out_h.element_size()
 
     peak, peak_src = hbm_peak()
-    achieved = kv_bytes / (kernel_ms / 1e3) / 1e9
     traffic, traffic_src = ncu_traffic(w.name)
     line = None
     if rank == 0:
@@ -372,16 +418,20 @@ def run_b200(args):
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True,
+            "scaling": "weak" if mode == "replicate" else "strong", "vs_baseline": None,
             "dtype": "bf16" if q.dtype == torch.bfloat16 else "f16", "data": "synthetic",
-            "config": {"workload": w.name, "description": w.description,
-                       "num_seqs_per_gpu": w.num_seqs, "num_q_heads": w.num_q_heads,
+            "config": {"workload": w.name, "description": w.description, "mode": mode,
+                       "num_seqs": w.num_seqs, "num_q_heads": w.num_q_heads,
                        "num_kv_heads": w.num_kv_heads, "head_size": w.head_size,
-                       "block_size": w.block_size, "kv_bytes_per_gpu_step": kv_bytes,
-                       "parallelism": f"dp{world} (independent sequence batches, no collective)",
-                       "l2": l2_note},
+                       "block_size": w.block_size, "kv_bytes_per_step_all_gpus": total_bytes,
+                       "kv_bytes_per_step_this_gpu": kv_bytes,
+                       "parallelism": parallelism, "l2": l2_note},
             "us_per_call": round(ms_per_step * 1e3, 2),
             "hbm_frac_of_measured_peak": round(value / world / peak, 4),
+            "gpu_launches_note": ("per step: planner, decode"
+                                  + (", reduce" if launches == 3 else "")
+                                  + (", state merge (+ NCCL all-gather)" if mode == "split" else "")),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "peak_source": peak_src,
@@ -394,7 +444,7 @@ def run_b200(args):
                     "note": "public wrapper; q, cache_seqlens, block_table H2D from pinned "
                             "memory and the output D2H every step; KV cache resident"},
             "clocks": sampler.summary(),
-            "gpu_launches": launches * K,
+            "gpu_launches": (launches + (1 if mode == "split" else 0)) * K,
         }
     if world > 1:
         barrier()
