@@ -234,7 +234,7 @@ def run_reference(args):
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_b200(args):
@@ -450,10 +450,26 @@ def run_b200(args):
         barrier()
         dist.destroy_process_group()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
+
+
+_json_out = None
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the process's original stdout."""
+    out = _json_out or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 def main():
+    global _json_out
+    # Libraries (NCCL, PyTorch) may print to stdout; keep stdout for the
+    # single JSON line by pointing file descriptor 1 at stderr.
+    sys.stdout.flush()
+    _json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
