@@ -343,14 +343,16 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int wpc = blockDim.x >> 5;
   const int depth = p.depth;
   const int gw = blockIdx.x * wpc + warp;
-  // Everything below reads what the planner wrote.
+  // Everything below reads what the planner wrote.  The three start-up
+  // values are independent loads, issued together (wstart has total_warps
+  // entries, so the read is in bounds even for a warp that then exits).
   grid_dependency_wait();
-  const int W = *p.weff;  // min(total_warps, total pages), set by the planner
-  if (gw >= W) return;
-
   const int n_heads = p.B * p.Hkv;
+  const int W = *p.weff;  // min(total_warps, total pages), set by the planner
   // Total pages < 2^31 (checked on the host), so page indices are 32-bit.
   const int total = p.cum[n_heads];
+  const int first_head = gw < p.total_warps ? p.wstart[gw] : 0;
+  if (gw >= W) return;
   if (total == 0) return;
   const int gs = static_cast<int>(static_cast<int64_t>(gw) * total / W);
   const int ge = static_cast<int>(static_cast<int64_t>(gw + 1) * total / W);
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       c_nspans = warp_of_page(c_hi - 1, total, W) - c_wfirst + 1;
     }
   };
-  load_window(p.wstart[gw]);
+  load_window(first_head);
   enter_head(win);
 
   int c_gp = gs;  // next global page to stage

@@ -136,3 +136,22 @@ def test_status_bits(cuda_device):
     st = read_status(dev)
     assert st & _lib.STATUS_NEG_SEQLEN and not st & _lib.STATUS_SEQLEN_CLAMP
     assert torch.count_nonzero(out[0]) == 0
+
+
+@pytest.mark.parametrize("core", ["0", "1"])
+def test_states_merge_both_arithmetic_paths(cuda_device, monkeypatch, core):
+    """Partial states written by the tensor-core and the CUDA-core variants
+    merge to the oracle's output."""
+    monkeypatch.setenv("PAB200_CORE", core)
+    B, Hkv, G, D, bs = 2, 2, 2, 128, 16
+    q, pk, pv, bt, lens, scale = _pool_case(B, Hkv, G, D, bs, [700, 90], torch.bfloat16, seed=9)
+    ref = run_oracle(*_reference_view(q, pk, pv, bt, lens), scale)[:, 0]
+    dev = cuda_device
+    starts, ends = context_ranges(lens, 3, 64)
+    S = state_numel(B, Hkv * G, D)
+    states = torch.empty((3, S), dtype=torch.float32, device=dev)
+    for r in range(3):
+        btl, ll = local_view(bt, lens, starts[r], ends[r], bs)
+        paged_attention_states(q.to(dev), pk.to(dev), pv.to(dev), btl.to(dev), ll.to(dev), scale,
+                               bs, state=states[r])
+    assert_close(merge_packed_states(states, B, Hkv * G, D), ref, what=f"core={core}")
