@@ -361,7 +361,43 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   return PAB200_OK;
 }
 
+int encode_cache_map_uncached(const pab200_decode_args* a, const void* base, CUtensorMap* map);
+
+// Tensor maps depend only on the cache pointer and its geometry; calls on the
+// same caches reuse the last few encodings instead of re-encoding per call.
 int encode_cache_map(const pab200_decode_args* a, const void* base, CUtensorMap* map) {
+  struct Entry {
+    const void* base;
+    int64_t pages;
+    int32_t dtype, layout, D, bs, hkv;
+    CUtensorMap map;
+  };
+  constexpr int kEntries = 8;
+  static Entry cache[kEntries];
+  static int used = 0, next = 0;
+  static std::mutex mu;
+  const int32_t hkv = a->layout == PAB200_LAYOUT_NHD ? a->num_kv_heads : 1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i) {
+      const Entry& e = cache[i];
+      if (e.base == base && e.pages == a->num_pages && e.dtype == a->dtype &&
+          e.layout == a->layout && e.D == a->head_size && e.bs == a->block_size && e.hkv == hkv) {
+        *map = e.map;
+        return PAB200_OK;
+      }
+    }
+  }
+  int rc = encode_cache_map_uncached(a, base, map);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  cache[next] = Entry{base, a->num_pages, a->dtype, a->layout, a->head_size, a->block_size, hkv, *map};
+  next = (next + 1) % kEntries;
+  if (used < kEntries) ++used;
+  return PAB200_OK;
+}
+
+int encode_cache_map_uncached(const pab200_decode_args* a, const void* base, CUtensorMap* map) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return fail(PAB200_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const int D = a->head_size;

@@ -144,8 +144,17 @@ def _run_decode(args: _lib.DecodeArgs, device: torch.device) -> None:
     _lib.check(lib, rc, "pab200_decode")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _current_stream_handle(device) -> int:
+    if _raw_stream is not None:  # cudaStream_t of the current stream, cheaply
+        return _raw_stream(device.index)
+    return torch.cuda.current_stream(device).cuda_stream
+
+
 def _launch(lib, args, device) -> int:
-    stream_handle = torch.cuda.current_stream(device).cuda_stream
+    stream_handle = _current_stream_handle(device)
     ws = _workspace(lib, args, device, stream_handle)
     rc = lib.pab200_decode(ctypes.byref(args), ws.data_ptr(), ws.numel(), stream_handle)
     if rc == _lib.ERR_WORKSPACE:
@@ -194,7 +203,8 @@ def flash_attn_with_kvcache_wrapper_b200(q, k_cache, v_cache, cache_seqlens, blo
         raise ValueError(f"cache head_size {k_cache.shape[2]} != q head_size {D}")
     if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
         raise ValueError("k_cache and v_cache must be contiguous")
-    if q.stride(3) != 1:
+    qs = q.stride()
+    if qs[3] != 1:
         raise ValueError("q must be contiguous in head_size")
     if num_splits < 0:
         raise ValueError("num_splits must be >= 0")
@@ -209,10 +219,10 @@ def flash_attn_with_kvcache_wrapper_b200(q, k_cache, v_cache, cache_seqlens, blo
     args.out = out.data_ptr()
     args.layout = _lib.LAYOUT_PAGES
     args.max_blocks = bt.shape[2]
-    args.q_stride_b, args.q_stride_h = q.stride(0), q.stride(2)
-    args.out_stride_b, args.out_stride_h = out.stride(0), out.stride(2)
-    args.seqlens_stride_b, args.seqlens_stride_h = lens.stride(0), lens.stride(1)
-    args.bt_stride_b, args.bt_stride_h, args.bt_stride_i = bt.stride(0), bt.stride(1), bt.stride(2)
+    args.q_stride_b, args.q_stride_h = qs[0], qs[2]
+    args.out_stride_b, args.out_stride_h = Hq * D, D   # fresh contiguous output
+    args.seqlens_stride_b, args.seqlens_stride_h = lens.stride()
+    args.bt_stride_b, args.bt_stride_h, args.bt_stride_i = bt.stride()
     args.bt_page_mul, args.bt_page_add = 1, 0
     _run_decode(args, device)
     return out
