@@ -218,6 +218,49 @@ int pab200_merge_states(const float* state_o, int64_t o_stride,
                         void* out, int64_t out_stride_row, int32_t out_dtype,
                         void* stream);
 
+/* Bytes of the exchange buffer each rank needs for pab200_exchange_merge():
+ * two parities of `world` packed states plus control words (flags, epoch).
+ * Each rank allocates its buffer once, zero-fills it, and maps every peer's
+ * buffer into its address space (CUDA IPC); all ranks must use the same
+ * `world`, `rows` and `head_size`. */
+size_t pab200_exchange_buffer_bytes(int32_t world, int64_t rows, int32_t head_size);
+
+/* Setup of the exchange buffers (once per process group and shape; these
+ * are the only calls of the library that allocate or map device memory).
+ *  create:  cudaMalloc `bytes` on the current device, zero-fill it, and write
+ *           its CUDA IPC handle (64 bytes) to `ipc_handle`.
+ *  open:    map a peer's buffer, given its handle, into this process on the
+ *           current device (peer access enabled on first use).
+ *  reset:   zero-fill a buffer (stream-ordered), e.g. on every rank after a
+ *           timed-out exchange.
+ *  close:   unmap a buffer mapped with open.
+ *  destroy: free a buffer made by create (after every peer closed it). */
+int pab200_exchange_buffer_create(size_t bytes, void** buf, void* ipc_handle);
+int pab200_exchange_buffer_open(const void* ipc_handle, void** peer_buf);
+int pab200_exchange_buffer_reset(void* buf, size_t bytes, void* stream);
+int pab200_exchange_buffer_close(void* peer_buf);
+int pab200_exchange_buffer_destroy(void* buf);
+
+/* Context split across the GPUs of one node, fused exchange + merge: the
+ * all-gather of partial states and the log-sum-exp merge of
+ * src/kernel_triton.py:120-174 in one kernel over peer memory.  `state` is
+ * this rank's packed state (o [rows, head_size] fp32, then lse [rows], the
+ * layout paged_attention_states writes, `rows` padded to a multiple of 4);
+ * `bufs` is a DEVICE array of `world` pointers to the exchange buffers of
+ * ranks 0..world-1 as mapped in this process (bufs[rank] is this rank's own).
+ * The kernel stores `state` into every rank's buffer over NVLink, publishes
+ * a per-call epoch flag to every rank (release, system scope), waits for
+ * every rank's flag of the same call (acquire; gives up after
+ * wait_limit_ns, sets PAB200_STATUS_WAIT_TIMEOUT in *status and merges what
+ * arrived), then writes out[rows, head_size] (row stride out_stride_row,
+ * type out_dtype) from its own memory.  Every rank must call it the same
+ * number of times; after a timeout the buffers must be zero-filled again on
+ * all ranks.  No multicast objects or multimem instructions are used. */
+int pab200_exchange_merge(const float* state, float* const* bufs, int32_t rank,
+                          int32_t world, int64_t rows, int32_t head_size,
+                          void* out, int64_t out_stride_row, int32_t out_dtype,
+                          int64_t wait_limit_ns, uint32_t* status, void* stream);
+
 /* Copy the device status word of `workspace` (the PAB200_STATUS_* bits raised
  * by the most recent pab200_decode call on it) to *status_out.  Synchronises
  * `stream`. */

@@ -47,6 +47,13 @@ EXPORTED_SYMBOLS = (
     "pab200_decode_noalloc",
     "pab200_paged_attention",
     "pab200_merge_states",
+    "pab200_exchange_buffer_bytes",
+    "pab200_exchange_buffer_create",
+    "pab200_exchange_buffer_open",
+    "pab200_exchange_buffer_reset",
+    "pab200_exchange_buffer_close",
+    "pab200_exchange_buffer_destroy",
+    "pab200_exchange_merge",
     "pab200_read_status",
     "pab200_strerror",
     "pab200_last_error",
@@ -131,6 +138,21 @@ def load() -> ctypes.CDLL:
         ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
         ctypes.c_void_p]
     lib.pab200_merge_states.restype = ctypes.c_int
+    lib.pab200_exchange_buffer_bytes.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]
+    lib.pab200_exchange_buffer_bytes.restype = ctypes.c_size_t
+    lib.pab200_exchange_buffer_create.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p),
+                                                  ctypes.c_void_p]
+    lib.pab200_exchange_buffer_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.pab200_exchange_buffer_reset.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.pab200_exchange_buffer_close.argtypes = [ctypes.c_void_p]
+    lib.pab200_exchange_buffer_destroy.argtypes = [ctypes.c_void_p]
+    for f in ("create", "open", "reset", "close", "destroy"):
+        getattr(lib, "pab200_exchange_buffer_" + f).restype = ctypes.c_int
+    lib.pab200_exchange_merge.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+        ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64,
+        ctypes.c_void_p, ctypes.c_void_p]
+    lib.pab200_exchange_merge.restype = ctypes.c_int
     lib.pab200_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32),
                                        ctypes.c_void_p]
     lib.pab200_read_status.restype = ctypes.c_int

@@ -1153,4 +1153,111 @@ __global__ void __launch_bounds__(256) merge_states_kernel(
   }
 }
 
+// --------------------------------------------------------------------------
+// Fused exchange + merge of partial states over peer memory (ranks of one
+// node, buffers mapped with CUDA IPC).  Replaces all-gather + merge_states for
+// a context split across GPUs: every rank stores its packed state into slot
+// [parity][rank] of every rank's exchange buffer (NVLink stores), publishes an
+// epoch flag with release semantics, waits (bounded) until every rank's flag
+// for this epoch is visible, and merges the world states from its own memory.
+//
+// Exchange buffer of each rank (floats): [2][world][S] state slots, then the
+// control words: flags[world] (last epoch received from each rank), epoch
+// (calls made by this rank), done (blocks finished copying in this call).
+// The two parities let a peer run one call ahead while this rank still reads
+// the previous call's slots; a peer cannot get two calls ahead because its
+// next exchange waits for this rank's flag.
+struct ExchangeParams {
+  const float* state;       // this rank's packed state: o [rows, D], lse [rows]
+  float* const* bufs;       // [world] exchange buffers as mapped here (bufs[rank] own)
+  int32_t rank, world;
+  int64_t S;                // floats per packed state (multiple of 4)
+  int64_t rows;
+  int32_t D;
+  void* out;
+  int64_t out_stride;
+  uint64_t wait_limit_ns;
+  uint32_t* status;         // PAB200_STATUS_* bits (timeout)
+};
+
+template <typename TO>
+__global__ void __launch_bounds__(256) exchange_merge_kernel(const ExchangeParams p) {
+  const int world = p.world, rank = p.rank;
+  const int64_t S = p.S;
+  const int tid = threadIdx.x;
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(p.bufs[rank] + 2 * world * S);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(ctrl + world) + 1u;
+  const int par = e & 1;
+  // 1. push the state to slot [par][rank] of every other rank (NVLink stores)
+  const float4* src = reinterpret_cast<const float4*>(p.state);
+  const int64_t n4 = S / 4;
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    float4* dst = reinterpret_cast<float4*>(p.bufs[r] + (static_cast<int64_t>(par) * world + rank) * S);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      dst[i] = src[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  // 2. the last block to finish copying publishes the epoch to every rank
+  if (tid == 0) {
+    const uint32_t done = atomicAdd(ctrl + world + 1, 1u);
+    if (done == gridDim.x - 1) {
+      ctrl[world + 1] = 0u;
+      ctrl[world] = e;
+      __threadfence_system();
+      for (int r = 0; r < world; ++r)
+        st_release_sys(reinterpret_cast<uint32_t*>(p.bufs[r] + 2 * world * S) + rank, e);
+    }
+  }
+  // 3. wait until every rank's state of epoch e has arrived (bounded)
+  if (tid < world) {
+    const uint32_t* f = ctrl + tid;
+    if (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
+      const uint64_t t0 = global_timer_ns();
+      while (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
+        if (global_timer_ns() - t0 > p.wait_limit_ns) {
+          atomicOr(p.status, kStatusTimeout);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // 4. merge: one warp per output row, lanes over the head dimension
+  const int lane = tid & 31;
+  // Slot i holds rank i's state; this rank's own is read from `state`.  Peer
+  // slots were written by other GPUs during this kernel, so they are read
+  // through L2 (ld.global.cg), never from a possibly stale L1 line.
+  const float* slots = p.bufs[rank] + static_cast<int64_t>(par) * world * S;
+  const int64_t rows = p.rows;
+  const int D = p.D;
+  auto slot = [&](int i) { return i == rank ? p.state : slots + i * S; };
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (tid >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.x) * 8) {
+    float M = -INFINITY;
+    for (int i = 0; i < world; ++i) M = fmaxf(M, __ldcg(slot(i) + rows * D + row));
+    for (int c = lane * 4; c < D; c += 128) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      float L = 0.f;
+      if (M != -INFINITY) {
+        for (int i = 0; i < world; ++i) {
+          const float* si = slot(i);
+          const float w = fast_exp2((__ldcg(si + rows * D + row) - M) * kLog2e);
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(si + row * D + c));
+          a.x += w * v.x;
+          a.y += w * v.y;
+          a.z += w * v.z;
+          a.w += w * v.w;
+          L += w;
+        }
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      store_out4<TO>(static_cast<TO*>(p.out) + row * p.out_stride + c,
+                     make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv));
+    }
+  }
+}
+
 }  // namespace pab

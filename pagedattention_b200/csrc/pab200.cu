@@ -14,6 +14,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "decode.cuh"
@@ -650,6 +651,118 @@ PAB200_EXPORT int pab200_merge_states(const float* state_o, int64_t o_stride,
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+  return PAB200_OK;
+}
+
+namespace {
+int64_t packed_state_floats(int64_t rows, int32_t head_size) {
+  return rows * head_size + ((rows + 3) / 4) * 4;
+}
+int64_t exchange_ctrl_floats(int32_t world) { return ((world + 2 + 3) / 4) * 4; }
+}  // namespace
+
+PAB200_EXPORT size_t pab200_exchange_buffer_bytes(int32_t world, int64_t rows, int32_t head_size) {
+  if (world < 1 || rows < 1 || head_size < 4 || (head_size & 3)) return 0;
+  return size_t(2 * world * packed_state_floats(rows, head_size) + exchange_ctrl_floats(world)) * 4;
+}
+
+PAB200_EXPORT int pab200_exchange_buffer_create(size_t bytes, void** buf, void* ipc_handle) {
+  if (!bytes || !buf || !ipc_handle) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer or size 0");
+  *buf = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (exchange buffer)");
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "exchange buffer setup");
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *buf = p;
+  return PAB200_OK;
+}
+
+PAB200_EXPORT int pab200_exchange_buffer_open(const void* ipc_handle, void** peer_buf) {
+  if (!ipc_handle || !peer_buf) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  *peer_buf = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return PAB200_OK;
+}
+
+PAB200_EXPORT int pab200_exchange_buffer_reset(void* buf, size_t bytes, void* stream) {
+  if (!buf) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaError_t e = cudaMemsetAsync(buf, 0, bytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PAB200_OK : cuda_fail(e, "cudaMemsetAsync");
+}
+
+PAB200_EXPORT int pab200_exchange_buffer_close(void* peer_buf) {
+  if (!peer_buf) return PAB200_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(peer_buf);
+  return e == cudaSuccess ? PAB200_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+PAB200_EXPORT int pab200_exchange_buffer_destroy(void* buf) {
+  if (!buf) return PAB200_OK;
+  cudaError_t e = cudaFree(buf);
+  return e == cudaSuccess ? PAB200_OK : cuda_fail(e, "cudaFree");
+}
+
+PAB200_EXPORT int pab200_exchange_merge(const float* state, float* const* bufs, int32_t rank,
+                                        int32_t world, int64_t rows, int32_t head_size, void* out,
+                                        int64_t out_stride_row, int32_t out_dtype,
+                                        int64_t wait_limit_ns, uint32_t* status, void* stream) {
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || rows < 1 || head_size < 4 ||
+      (head_size & 3) || wait_limit_ns <= 0)
+    return fail(PAB200_ERR_INVALID_ARGUMENT,
+                "need 0 <= rank < world <= 64, rows >= 1, head_size %% 4 == 0, wait_limit_ns > 0");
+  if (!state || !bufs || !out || !status) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  const size_t oal = out_dtype == PAB200_DTYPE_F32 ? 16 : 8;
+  if (!aligned(state, 16) || !aligned(out, oal) || (out_stride_row & 3) || !aligned(status, 4))
+    return fail(PAB200_ERR_ALIGNMENT, "state 16-byte, out %zu-byte aligned, out_stride_row %% 4 == 0",
+                oal);
+  pab::ExchangeParams p{};
+  p.state = state;
+  p.bufs = bufs;
+  p.rank = rank;
+  p.world = world;
+  p.S = packed_state_floats(rows, head_size);
+  p.rows = rows;
+  p.D = head_size;
+  p.out = out;
+  p.out_stride = out_stride_row;
+  p.wait_limit_ns = static_cast<uint64_t>(wait_limit_ns);
+  p.status = status;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  sms = device_sm_count(dev);
+  // Blocks wait for one another's copies through the epoch flags, so the
+  // grid stays well under one block per SM (all blocks resident).
+  int64_t blocks = (rows + 7) / 8;
+  const int64_t cap = sms > 2 ? sms / 2 : 1;
+  if (blocks > cap) blocks = cap;
+  const dim3 grid(static_cast<unsigned>(blocks)), block(256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (out_dtype) {
+    case PAB200_DTYPE_BF16:
+      pab::exchange_merge_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(p);
+      break;
+    case PAB200_DTYPE_F16:
+      pab::exchange_merge_kernel<__half><<<grid, block, 0, s>>>(p);
+      break;
+    case PAB200_DTYPE_F32:
+      pab::exchange_merge_kernel<float><<<grid, block, 0, s>>>(p);
+      break;
+    default:
+      return fail(PAB200_ERR_UNSUPPORTED, "out_dtype %d", out_dtype);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "exchange kernel launch");
   return PAB200_OK;
 }
 

@@ -13,18 +13,27 @@ The decode path spreads over devices in two ways:
   (num_seqs * num_q_heads * (head_size + 1) floats per rank), and
   ``merge_packed_states`` combines them: the reference's log-sum-exp reduce
   (src/kernel_triton.py:120-174) applied across devices.  Any rank's
-  output is the full-context result.
+  output is the full-context result.  With a ``PeerExchange`` the gather and
+  the merge are one kernel over peer memory instead (NVLink stores into
+  every rank's exchange buffer, mapped with CUDA IPC; an epoch flag per rank;
+  a bounded wait), which saves the NCCL launch and the separate merge.
 
 The reference has no multi-device code; this module is new.
 """
 from __future__ import annotations
 
+import ctypes
 import heapq
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .kernel_b200 import merge_packed_states, paged_attention_states, state_numel
+
+_OUT_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16,
+               torch.float32: _lib.DTYPE_F32}
+IPC_HANDLE_BYTES = 64
 
 
 def shard_sequences(lens, world_size: int) -> list[list[int]]:
@@ -90,19 +99,147 @@ def all_gather_states(state: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+class PeerExchange:
+    """Exchange buffers of the ranks of one node for the fused exchange +
+    merge (``pab200_exchange_merge``), mapped into every rank with CUDA IPC.
+
+    Collective: every rank of ``group`` constructs it with the same shape,
+    on its own current CUDA device (one process per GPU).  Each rank's
+    buffer holds two parities of ``world`` packed states plus control words;
+    the handles travel once through ``all_gather_object``.  ``wait_limit_s``
+    bounds the wait for peers inside the kernel: when it runs out the kernel
+    sets ``STATUS_WAIT_TIMEOUT`` in ``status`` and merges what arrived, and
+    all ranks must then call ``reset()`` before the next exchange.  Every
+    rank must make the same sequence of exchange calls.
+    """
+
+    def __init__(self, num_seqs: int, num_q_heads: int, head_size: int, group=None,
+                 wait_limit_s: float = 1.0):
+        self.lib = lib = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.shape = (num_seqs, num_q_heads, head_size)
+        self.rows = num_seqs * num_q_heads
+        self.nbytes = lib.pab200_exchange_buffer_bytes(self.world, self.rows, head_size)
+        if not self.nbytes:
+            raise ValueError(f"unsupported exchange shape {self.shape} for world {self.world}")
+        self.wait_limit_ns = max(int(wait_limit_s * 1e9), 1)
+        buf = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib, lib.pab200_exchange_buffer_create(self.nbytes, ctypes.byref(buf),
+                                                              handle),
+                       "pab200_exchange_buffer_create")
+        self._own = buf.value
+        self._opened: list[int] = []
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs = []
+        try:
+            with torch.cuda.device(self.device):
+                for r, h in enumerate(handles):
+                    if r == self.rank:
+                        ptrs.append(self._own)
+                        continue
+                    pb = ctypes.c_void_p()
+                    hb = (ctypes.c_ubyte * IPC_HANDLE_BYTES).from_buffer_copy(h)
+                    _lib.check(lib, lib.pab200_exchange_buffer_open(hb, ctypes.byref(pb)),
+                               "pab200_exchange_buffer_open")
+                    self._opened.append(pb.value)
+                    ptrs.append(pb.value)
+        except Exception:
+            self._release()
+            raise
+        self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.state = torch.empty(state_numel(*self.shape), dtype=torch.float32,
+                                 device=self.device)
+        dist.barrier(group)
+
+    def exchange_merge(self, state: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Merge every rank's packed ``state`` into ``out`` (num_seqs,
+        num_q_heads, head_size), on the current stream."""
+        code = _OUT_DTYPES.get(out.dtype)
+        if code is None:
+            raise TypeError(f"unsupported out dtype {out.dtype}")
+        if (tuple(out.shape) != self.shape or not out.is_contiguous()
+                or out.device != self.device):
+            raise ValueError(f"out must be a contiguous {self.shape} tensor on {self.device}")
+        if (state.dtype != torch.float32 or not state.is_contiguous()
+                or state.numel() < state_numel(*self.shape) or state.device != self.device):
+            raise ValueError("state must be a contiguous float32 tensor of state_numel() elements")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = self.lib.pab200_exchange_merge(
+            ctypes.c_void_p(state.data_ptr()), ctypes.c_void_p(self.bufs.data_ptr()), self.rank,
+            self.world, self.rows, self.shape[2], ctypes.c_void_p(out.data_ptr()), self.shape[2],
+            code, self.wait_limit_ns, ctypes.c_void_p(self.status.data_ptr()),
+            ctypes.c_void_p(stream))
+        _lib.check(self.lib, rc, "pab200_exchange_merge")
+        return out
+
+    def read_status(self) -> int:
+        """Status bits of the exchanges so far (synchronises the device)."""
+        return int(self.status.item()) & 0xFFFFFFFF
+
+    def reset(self) -> None:
+        """Zero this rank's buffer and status; collective (all ranks, with no
+        exchange in flight), e.g. after a timed-out exchange."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(self.lib, self.lib.pab200_exchange_buffer_reset(
+            ctypes.c_void_p(self._own), self.nbytes, ctypes.c_void_p(stream)),
+            "pab200_exchange_buffer_reset")
+        self.status.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+
+    def _release(self) -> None:
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self.lib.pab200_exchange_buffer_close(ctypes.c_void_p(p))
+            self._opened = []
+            if self._own:
+                self.lib.pab200_exchange_buffer_destroy(ctypes.c_void_p(self._own))
+                self._own = None
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's; collective."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self.lib.pab200_exchange_buffer_close(ctypes.c_void_p(p))
+        self._opened = []
+        dist.barrier(self.group)
+        self._release()
+
+
 def decode_context_parallel(query, key_cache, value_cache, block_tables, context_lens, scale,
-                            block_size, group=None, kv_layout="HND", out=None):
+                            block_size, group=None, kv_layout="HND", out=None, exchange=None):
     """Decode with every sequence's context split across the ranks of ``group``.
 
     Each rank passes ITS token range: block_tables / context_lens describe
     only the pages it holds (see ``local_view``), query is the full query on
     every rank.  Returns out (num_seqs, num_q_heads, head_size) in query's
-    dtype, identical on all ranks.
+    dtype, identical on all ranks.  ``exchange`` (a ``PeerExchange`` of this
+    shape) replaces the NCCL all-gather + merge with the fused kernel over
+    peer memory.
     """
     B, Hq, D = query.shape
-    S = state_numel(B, Hq, D)
-    state = torch.empty(S, dtype=torch.float32, device=query.device)
+    if exchange is not None:
+        state = exchange.state
+    else:
+        state = torch.empty(state_numel(B, Hq, D), dtype=torch.float32, device=query.device)
     paged_attention_states(query, key_cache, value_cache, block_tables, context_lens, scale,
                            block_size, kv_layout=kv_layout, state=state)
+    if exchange is not None:
+        if out is None:
+            out = torch.empty((B, Hq, D), dtype=query.dtype, device=query.device)
+        return exchange.exchange_merge(state, out)
     gathered = all_gather_states(state, group)
     return merge_packed_states(gathered, B, Hq, D, out=out, out_dtype=query.dtype)
