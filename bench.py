@@ -53,6 +53,10 @@ def parse_args():
                     help="wall budget of the CPU-baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="split mode's state exchange: p2p = one fused kernel that stores the "
+                         "states into peer memory and merges (CUDA IPC buffers); nccl = NCCL "
+                         "all-gather, then the merge kernel")
     ap.add_argument("--mode", choices=["replicate", "shard", "split"], default=None,
                     help="N>1: replicate = every rank its own batch (weak scaling); shard = "
                          "one batch's sequences split over ranks (strong); split = every "
@@ -242,8 +246,8 @@ def run_b200(args):
     import torch.distributed as dist
 
     from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode
-    from pagedattention_b200.distributed import (context_ranges, decode_context_parallel,
-                                                 shard_sequences)
+    from pagedattention_b200.distributed import (PeerExchange, context_ranges,
+                                                 decode_context_parallel, shard_sequences)
     from pagedattention_b200.kernel_b200 import kernel_events, launches_per_call
     from pagedattention_b200.workloads import WORKLOADS, make_inputs, sample_lens
 
@@ -286,7 +290,10 @@ def run_b200(args):
         inp = make_inputs(w, seed=args.seed, device=dev, gen_device=dev,
                           lens=(ends[rank] - starts[rank]).to(torch.int32))
         parallelism = (f"context split over {world} ranks ({w.partition_tokens or 512}-token "
-                       "aligned ranges), (o, lse) states all-gathered over NCCL and merged")
+                       "aligned ranges), " + (
+                           "(o, lse) states stored into peer memory and merged by one fused "
+                           "kernel" if args.exchange == "p2p" else
+                           "(o, lse) states all-gathered over NCCL and merged"))
     q, k, v, sl, bt = inp.reference_layout()
     bt = bt.contiguous()
     kv_bytes = inp.kv_bytes()
@@ -306,6 +313,9 @@ def run_b200(args):
                    f"rotate over {copies} copies of the cache ({copies * kv_bytes / 2**20:.0f} MiB "
                    f"of KV read per rotation)")
     step_no = [0]
+    exchange = None
+    if mode == "split" and args.exchange == "p2p":
+        exchange = PeerExchange(*q[:, 0].shape)
 
     kpool_copies = [(inp.k_pool, inp.v_pool)] + [
         (kc.view_as(inp.k_pool), vc.view_as(inp.v_pool)) for kc, vc in caches[1:]]
@@ -316,7 +326,7 @@ def run_b200(args):
         if mode == "split":
             kp, vp = kpool_copies[i]
             return decode_context_parallel(qx[:, 0], kp, vp, seq_bt, seq_lens, inp.scale,
-                                           w.block_size)
+                                           w.block_size, exchange=exchange)
         kc, vc = caches[i]
         return decode(qx, kc, vc, slx, btx, inp.scale)
 
@@ -427,6 +437,12 @@ def run_b200(args):
     h2d = sum(h.numel() * h.element_size() for h in hosts)
     d2h = out_h[0].numel() * out_h[0].element_size()
 
+    exchange_status = None
+    if exchange is not None:
+        exchange_status = exchange.read_status()
+        exchange.close()
+        if exchange_status:
+            raise SystemExit(f"rank {rank}: peer exchange status {exchange_status:#x}")
     peak, peak_src = hbm_peak()
     traffic, traffic_src = ncu_traffic(w.name)
     line = None
@@ -453,7 +469,9 @@ def run_b200(args):
             "hbm_frac_of_measured_peak": round(value / world / peak, 4),
             "gpu_launches_note": ("per step: planner, decode"
                                   + (", reduce" if launches == 3 else "")
-                                  + (", state merge (+ NCCL all-gather)" if mode == "split" else "")),
+                                  + ((", fused state exchange + merge" if exchange is not None
+                                      else ", state merge (+ NCCL all-gather)")
+                                     if mode == "split" else "")),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "peak_source": peak_src,

@@ -219,10 +219,11 @@ int pab200_merge_states(const float* state_o, int64_t o_stride,
                         void* stream);
 
 /* Bytes of the exchange buffer each rank needs for pab200_exchange_merge():
- * two parities of `world` packed states plus control words (flags, epoch).
- * Each rank allocates its buffer once, zero-fills it, and maps every peer's
- * buffer into its address space (CUDA IPC); all ranks must use the same
- * `world`, `rows` and `head_size`. */
+ * two parities of `world` packed states, every float stored as a 64-bit
+ * {value, epoch} word, plus one epoch counter per exchange block.  Each rank
+ * allocates its buffer once (pab200_exchange_buffer_create, zero-filled) and
+ * maps every peer's buffer into its address space (CUDA IPC); all ranks must
+ * use the same `world`, `rows` and `head_size`. */
 size_t pab200_exchange_buffer_bytes(int32_t world, int64_t rows, int32_t head_size);
 
 /* Setup of the exchange buffers (once per process group and shape; these
@@ -248,15 +249,16 @@ int pab200_exchange_buffer_destroy(void* buf);
  * layout paged_attention_states writes, `rows` padded to a multiple of 4);
  * `bufs` is a DEVICE array of `world` pointers to the exchange buffers of
  * ranks 0..world-1 as mapped in this process (bufs[rank] is this rank's own).
- * The kernel stores `state` into every rank's buffer over NVLink, publishes
- * a per-call epoch flag to every rank (release, system scope), waits for
- * every rank's flag of the same call (acquire; gives up after
- * wait_limit_ns, sets PAB200_STATUS_WAIT_TIMEOUT in *status and merges what
- * arrived), then writes out[rows, head_size] (row stride out_stride_row,
- * type out_dtype) from its own memory.  Every rank must call it the same
- * number of times; after a timeout the buffers must be zero-filled again on
- * all ranks.  No multicast objects or multimem instructions are used. */
-int pab200_exchange_merge(const float* state, float* const* bufs, int32_t rank,
+ * The kernel stores `state` into every peer's buffer over NVLink, each value
+ * in one 64-bit word with the call's epoch, then writes out[rows, head_size]
+ * (row stride out_stride_row, type out_dtype) from its own memory once every
+ * peer's words of the same call have arrived.  A wait longer than
+ * wait_limit_ns sets PAB200_STATUS_WAIT_TIMEOUT in *status and merges what
+ * is there.  Every rank must call it the same number of times; after a
+ * timeout all ranks must zero their buffers (pab200_exchange_buffer_reset)
+ * before the next call.  No multicast objects or multimem instructions are
+ * used. */
+int pab200_exchange_merge(const float* state, void* const* bufs, int32_t rank,
                           int32_t world, int64_t rows, int32_t head_size,
                           void* out, int64_t out_stride_row, int32_t out_dtype,
                           int64_t wait_limit_ns, uint32_t* status, void* stream);

@@ -1156,100 +1156,138 @@ __global__ void __launch_bounds__(256) merge_states_kernel(
 // --------------------------------------------------------------------------
 // Fused exchange + merge of partial states over peer memory (ranks of one
 // node, buffers mapped with CUDA IPC).  Replaces all-gather + merge_states for
-// a context split across GPUs: every rank stores its packed state into slot
-// [parity][rank] of every rank's exchange buffer (NVLink stores), publishes an
-// epoch flag with release semantics, waits (bounded) until every rank's flag
-// for this epoch is visible, and merges the world states from its own memory.
+// a context split across GPUs.
 //
-// Exchange buffer of each rank (floats): [2][world][S] state slots, then the
-// control words: flags[world] (last epoch received from each rank), epoch
-// (calls made by this rank), done (blocks finished copying in this call).
-// The two parities let a peer run one call ahead while this rank still reads
-// the previous call's slots; a peer cannot get two calls ahead because its
-// next exchange waits for this rank's flag.
+// Every value crosses NVLink as one 64-bit word {float bits, epoch}, stored
+// and loaded with relaxed system-scope accesses (single-copy atomic), so a
+// reader that sees the current epoch in a word also sees its value: no fence,
+// no separate flag and no second NVLink trip.  Block b of every rank owns the
+// same rows [r0, r1): it stores this rank's o and lse of those rows into slot
+// [parity][rank] of every peer's buffer, then merges the rows, waiting
+// (bounded) for each peer word of the current epoch in its own memory.
+//
+// Exchange buffer of each rank: [2][world][S] uint64 words, then uint32
+// epoch[nb] (calls block b has made; nb = exchange_blocks(rows), the same on
+// every rank).  The two parities let a peer run one call ahead while this
+// rank still reads the previous call's slots; a peer cannot get two calls
+// ahead because its next call waits for this rank's words of the call in
+// between, which this rank stores only after finishing the current one.
 struct ExchangeParams {
   const float* state;       // this rank's packed state: o [rows, D], lse [rows]
-  float* const* bufs;       // [world] exchange buffers as mapped here (bufs[rank] own)
+  uint64_t* const* bufs;    // [world] exchange buffers as mapped here (bufs[rank] own)
   int32_t rank, world;
   int64_t S;                // floats per packed state (multiple of 4)
   int64_t rows;
   int32_t D;
+  int64_t rows_per_block;
   void* out;
   int64_t out_stride;
   uint64_t wait_limit_ns;
   uint32_t* status;         // PAB200_STATUS_* bits (timeout)
 };
 
-template <typename TO>
-__global__ void __launch_bounds__(256) exchange_merge_kernel(const ExchangeParams p) {
-  const int world = p.world, rank = p.rank;
-  const int64_t S = p.S;
-  const int tid = threadIdx.x;
-  uint32_t* ctrl = reinterpret_cast<uint32_t*>(p.bufs[rank] + 2 * world * S);
-  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(ctrl + world) + 1u;
-  const int par = e & 1;
-  // 1. push the state to slot [par][rank] of every other rank (NVLink stores)
-  const float4* src = reinterpret_cast<const float4*>(p.state);
-  const int64_t n4 = S / 4;
-  for (int r = 0; r < world; ++r) {
-    if (r == rank) continue;
-    float4* dst = reinterpret_cast<float4*>(p.bufs[r] + (static_cast<int64_t>(par) * world + rank) * S);
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < n4;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-      dst[i] = src[i];
+__host__ __device__ inline int64_t exchange_blocks(int64_t rows) {
+  const int64_t nb = (rows + 7) / 8;
+  return nb < 128 ? nb : 128;
+}
+
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t e) {
+  return (static_cast<uint64_t>(e) << 32) | __float_as_uint(v);
+}
+
+// Loads N words at p[0], p[step], ... once all carry epoch e.  On timeout
+// sets the status bit, stops waiting for the rest of this thread's loads
+// (`gave_up`) and returns what is there.
+template <int N>
+__device__ __forceinline__ void ll_load(const uint64_t* p, int64_t step, uint32_t e, float* v,
+                                        bool& gave_up, const ExchangeParams& prm) {
+  uint64_t w[N];
+  bool ready = true;
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    w[k] = ld_relaxed_sys_u64(p + k * step);
+    ready &= static_cast<uint32_t>(w[k] >> 32) == e;
   }
-  __threadfence_system();
-  __syncthreads();
-  // 2. the last block to finish copying publishes the epoch to every rank
-  if (tid == 0) {
-    const uint32_t done = atomicAdd(ctrl + world + 1, 1u);
-    if (done == gridDim.x - 1) {
-      ctrl[world + 1] = 0u;
-      ctrl[world] = e;
-      __threadfence_system();
-      for (int r = 0; r < world; ++r)
-        st_release_sys(reinterpret_cast<uint32_t*>(p.bufs[r] + 2 * world * S) + rank, e);
-    }
-  }
-  // 3. wait until every rank's state of epoch e has arrived (bounded)
-  if (tid < world) {
-    const uint32_t* f = ctrl + tid;
-    if (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
-      const uint64_t t0 = global_timer_ns();
-      while (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
-        if (global_timer_ns() - t0 > p.wait_limit_ns) {
-          atomicOr(p.status, kStatusTimeout);
-          break;
-        }
+  if (!ready && !gave_up) {
+    const uint64_t t0 = global_timer_ns();
+    while (!ready) {
+      ready = true;
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        if (static_cast<uint32_t>(w[k] >> 32) != e) w[k] = ld_relaxed_sys_u64(p + k * step);
+        ready &= static_cast<uint32_t>(w[k] >> 32) == e;
+      }
+      if (!ready && global_timer_ns() - t0 > prm.wait_limit_ns) {
+        atomicOr(prm.status, kStatusTimeout);
+        gave_up = true;
+        break;
       }
     }
   }
-  __syncthreads();
-  // 4. merge: one warp per output row, lanes over the head dimension
-  const int lane = tid & 31;
-  // Slot i holds rank i's state; this rank's own is read from `state`.  Peer
-  // slots were written by other GPUs during this kernel, so they are read
-  // through L2 (ld.global.cg), never from a possibly stale L1 line.
-  const float* slots = p.bufs[rank] + static_cast<int64_t>(par) * world * S;
-  const int64_t rows = p.rows;
+#pragma unroll
+  for (int k = 0; k < N; ++k) v[k] = __uint_as_float(static_cast<uint32_t>(w[k]));
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(256) exchange_merge_kernel(const ExchangeParams p) {
+  const int world = p.world, rank = p.rank;
+  const int64_t S = p.S, rows = p.rows;
   const int D = p.D;
-  auto slot = [&](int i) { return i == rank ? p.state : slots + i * S; };
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (tid >> 5); row < rows;
-       row += static_cast<int64_t>(gridDim.x) * 8) {
+  const int tid = threadIdx.x, b = blockIdx.x;
+  const int64_t r0 = b * p.rows_per_block;
+  const int64_t r1 = r0 + p.rows_per_block < rows ? r0 + p.rows_per_block : rows;
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(p.bufs[rank] + 2 * world * S);
+  // `state` (and, after a previous exchange, `epochs`) were written by the
+  // preceding grid on this stream: read them only after it has completed
+  grid_dependency_wait();
+  const uint32_t e = reinterpret_cast<volatile uint32_t*>(epochs)[b] + 1u;
+  const int par = e & 1;
+  // 1. store rows [r0, r1) of o and lse into every peer's slot [par][rank]
+  const float* st = p.state;
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    uint64_t* slot = p.bufs[r] + (static_cast<int64_t>(par) * world + rank) * S;
+    for (int64_t i = r0 * D + 2 * tid; i < r1 * D; i += 2 * blockDim.x) {
+      const float2 v = *reinterpret_cast<const float2*>(st + i);
+      st_relaxed_sys_u64(slot + i, ll_word(v.x, e));
+      st_relaxed_sys_u64(slot + i + 1, ll_word(v.y, e));
+    }
+    for (int64_t i = rows * D + r0 + tid; i < rows * D + r1; i += blockDim.x)
+      st_relaxed_sys_u64(slot + i, ll_word(st[i], e));
+  }
+  if (tid == 0) epochs[b] = e;  // read only by this block's next call
+  // 2. merge rows [r0, r1): one warp per row, lanes over the head dimension;
+  //    slot i holds rank i's words, this rank's own state is read directly
+  const int lane = tid & 31;
+  const uint64_t* slots = p.bufs[rank] + static_cast<int64_t>(par) * world * S;
+  bool gave_up = false;
+  for (int64_t row = r0 + (tid >> 5); row < r1; row += blockDim.x / 32) {
     float M = -INFINITY;
-    for (int i = 0; i < world; ++i) M = fmaxf(M, __ldcg(slot(i) + rows * D + row));
+    for (int i = 0; i < world; ++i) {
+      float l;
+      if (i == rank) l = st[rows * D + row];
+      else ll_load<1>(slots + i * S + rows * D + row, 1, e, &l, gave_up, p);
+      M = fmaxf(M, l);
+    }
     for (int c = lane * 4; c < D; c += 128) {
       float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
       float L = 0.f;
       if (M != -INFINITY) {
         for (int i = 0; i < world; ++i) {
-          const float* si = slot(i);
-          const float w = fast_exp2((__ldcg(si + rows * D + row) - M) * kLog2e);
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(si + row * D + c));
-          a.x += w * v.x;
-          a.y += w * v.y;
-          a.z += w * v.z;
-          a.w += w * v.w;
+          float l, v[4];
+          if (i == rank) {
+            l = st[rows * D + row];
+            const float4 o = *reinterpret_cast<const float4*>(st + row * D + c);
+            v[0] = o.x, v[1] = o.y, v[2] = o.z, v[3] = o.w;
+          } else {
+            ll_load<1>(slots + i * S + rows * D + row, 1, e, &l, gave_up, p);
+            ll_load<4>(slots + i * S + row * D + c, 1, e, v, gave_up, p);
+          }
+          const float w = fast_exp2((l - M) * kLog2e);
+          a.x += w * v[0];
+          a.y += w * v[1];
+          a.z += w * v[2];
+          a.w += w * v[3];
           L += w;
         }
       }

@@ -658,12 +658,13 @@ namespace {
 int64_t packed_state_floats(int64_t rows, int32_t head_size) {
   return rows * head_size + ((rows + 3) / 4) * 4;
 }
-int64_t exchange_ctrl_floats(int32_t world) { return ((world + 2 + 3) / 4) * 4; }
+int64_t exchange_epoch_words(int64_t rows) { return ((pab::exchange_blocks(rows) + 3) / 4) * 4; }
 }  // namespace
 
 PAB200_EXPORT size_t pab200_exchange_buffer_bytes(int32_t world, int64_t rows, int32_t head_size) {
   if (world < 1 || rows < 1 || head_size < 4 || (head_size & 3)) return 0;
-  return size_t(2 * world * packed_state_floats(rows, head_size) + exchange_ctrl_floats(world)) * 4;
+  return size_t(2 * world * packed_state_floats(rows, head_size)) * 8 +
+         size_t(exchange_epoch_words(rows)) * 4;
 }
 
 PAB200_EXPORT int pab200_exchange_buffer_create(size_t bytes, void** buf, void* ipc_handle) {
@@ -712,7 +713,7 @@ PAB200_EXPORT int pab200_exchange_buffer_destroy(void* buf) {
   return e == cudaSuccess ? PAB200_OK : cuda_fail(e, "cudaFree");
 }
 
-PAB200_EXPORT int pab200_exchange_merge(const float* state, float* const* bufs, int32_t rank,
+PAB200_EXPORT int pab200_exchange_merge(const float* state, void* const* bufs, int32_t rank,
                                         int32_t world, int64_t rows, int32_t head_size, void* out,
                                         int64_t out_stride_row, int32_t out_dtype,
                                         int64_t wait_limit_ns, uint32_t* status, void* stream) {
@@ -727,7 +728,7 @@ PAB200_EXPORT int pab200_exchange_merge(const float* state, float* const* bufs, 
                 oal);
   pab::ExchangeParams p{};
   p.state = state;
-  p.bufs = bufs;
+  p.bufs = reinterpret_cast<uint64_t* const*>(bufs);
   p.rank = rank;
   p.world = world;
   p.S = packed_state_floats(rows, head_size);
@@ -737,31 +738,30 @@ PAB200_EXPORT int pab200_exchange_merge(const float* state, float* const* bufs, 
   p.out_stride = out_stride_row;
   p.wait_limit_ns = static_cast<uint64_t>(wait_limit_ns);
   p.status = status;
-  int dev = 0, sms = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  sms = device_sm_count(dev);
-  // Blocks wait for one another's copies through the epoch flags, so the
-  // grid stays well under one block per SM (all blocks resident).
-  int64_t blocks = (rows + 7) / 8;
-  const int64_t cap = sms > 2 ? sms / 2 : 1;
-  if (blocks > cap) blocks = cap;
-  const dim3 grid(static_cast<unsigned>(blocks)), block(256);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Every rank uses the same grid: block b owns rows [b*rpb, (b+1)*rpb) on
+  // all ranks and waits only for the peers' block b.
+  const int64_t blocks = pab::exchange_blocks(rows);
+  p.rows_per_block = (rows + blocks - 1) / blocks;
+  // Programmatic dependent launch: the grid is scheduled while the kernel
+  // that writes `state` drains, and waits for it (griddepcontrol.wait)
+  // before the first read.
+  LaunchCfg lc(dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+               static_cast<cudaStream_t>(stream), true);
+  cudaError_t e;
   switch (out_dtype) {
     case PAB200_DTYPE_BF16:
-      pab::exchange_merge_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(p);
+      e = cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<__nv_bfloat16>, p);
       break;
     case PAB200_DTYPE_F16:
-      pab::exchange_merge_kernel<__half><<<grid, block, 0, s>>>(p);
+      e = cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<__half>, p);
       break;
     case PAB200_DTYPE_F32:
-      pab::exchange_merge_kernel<float><<<grid, block, 0, s>>>(p);
+      e = cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<float>, p);
       break;
     default:
       return fail(PAB200_ERR_UNSUPPORTED, "out_dtype %d", out_dtype);
   }
-  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "exchange kernel launch");
   return PAB200_OK;
 }
