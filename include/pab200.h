@@ -139,17 +139,17 @@ typedef struct pab200_decode_args {
 size_t pab200_decode_workspace_size(const pab200_decode_args* args);
 
 /* Number of kernel launches pab200_decode() makes for these arguments on the
- * current device: 2 (planner, decode with split heads merged in place) or 3
- * (plus a reduce kernel when the split heads' partial states are large);
- * 0 if the arguments are invalid.  The reference makes 2 (plus host work,
- * src/kernel_triton.py:245-305). */
+ * current device: 3 (planner, decode, reduce), or 0 if the arguments are
+ * invalid.  The reference makes 2 (plus host work, src/kernel_triton.py:
+ * 245-305). */
 int pab200_decode_launch_count(const pab200_decode_args* args);
 
 /* Paged-attention decode.  Replaces flash_attn_with_kvcache_wrapper_triton
  * (src/kernel_triton.py:181-307: planner + split kernel + reduce kernel) with
  * launches on `stream`: a device-side planner (no host sync), the split-KV
- * decode kernel (which merges split heads itself when their partial states
- * are small) and, otherwise, a log-sum-exp reduce kernel.  `workspace` is a device buffer
+ * decode kernel and a log-sum-exp reduce kernel for heads split across warps
+ * (scheduled early by programmatic dependent launch).  Results do not depend
+ * on run-time scheduling: repeated calls are bit-identical.  `workspace` is a device buffer
  * of at least pab200_decode_workspace_size() bytes, 256-byte aligned; its
  * contents need no initialisation.  `stream` is a cudaStream_t (0 = legacy
  * default stream). */

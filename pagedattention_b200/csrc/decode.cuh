@@ -14,18 +14,29 @@
 //   decode_kernel  persistent.  The concatenation of all heads' pages is cut
 //                  into W equal contiguous ranges, one per warp (W = every
 //                  resident warp on the device), so the load is balanced to a
-//                  page whatever the length mix.  Each warp streams its pages
+//                  page whatever the length mix.  The last `m` chunks of `K`
+//                  pages of every range are claimed at run time (one 64-bit
+//                  atomic word per warp): the owner takes them from the front,
+//                  warps that ran out of work steal them from the back, which
+//                  evens out the speed differences between warps (SM position,
+//                  HBM channel mix) that a static split leaves as a tail.
+//                  Each warp streams its pages
 //                  through a private ring of shared-memory stages filled by
 //                  tensor-map bulk copies (TMA, 128-byte swizzle, mbarrier
 //                  completion), computes S^T = K Q^T and O^T += V^T P^T with
 //                  mma.sync m16n8k16 (tokens are the M dimension, the G query
 //                  heads of one kv head the N dimension, so one K/V read
 //                  serves the whole group) and keeps an online softmax in
-//                  registers.  A head covered by one warp is written directly;
-//                  a head split over several warps has each warp write a
-//                  partial (max, sum, acc) and the last one to finish (atomic
-//                  ticket) merges them — the reduce kernel of the reference,
-//                  fused.
+//                  registers.  A head lying wholly in one segment (the static
+//                  prefix or one chunk of a range) is written directly; a
+//                  head split over several segments has each segment write a
+//                  partial (max, sum, acc) with plain stores.  Segments,
+//                  partials and merge order are fixed by the page counts
+//                  alone, so results do not depend on which warp ran which
+//                  chunk.
+//   reduce_kernel  one CTA per split head merges its partial states (the
+//                  reduce kernel of the reference), scheduled early through
+//                  programmatic dependent launch.
 //
 // Shared-memory stage layout (per warp, per ring slot), ST tokens:
 //   K: [D/64 planes][ST rows][128 bytes], then V with the same shape.
@@ -72,14 +83,18 @@ struct DecodeParams {
   // workspace
   int32_t* cum;       // [n_heads + 1] exclusive prefix of page counts
   int32_t* wstart;    // [W] first head of each warp's page range
-  uint32_t* tickets;  // [n_heads] arrivals of split heads (reset by planner)
   uint32_t* status;   // [1] PAB200_STATUS_* bits
   int32_t* weff;      // [1] warps in use: min(total_warps, total pages)
-  float* part;        // [(n_heads + W) * slot_floats] partial states
+  // [4] dynamic tail, written by the planner: m (tail chunks per warp), K
+  // (pages per chunk), chunks left to claim, thief cursor
+  int32_t* steal;
+  unsigned long long* claims;  // [W] claim words: low 32 bits front, high back
+  int32_t steal_m_max;         // tail chunks per warp the workspace holds
+  int32_t steal_pps;           // pages per ring stage (ST / block_size)
+  // [(n_heads + W * (steal_m_max + 1)) * slot_floats] partial states, one
+  // per (head, segment) pair; slot layout: acc [G][D], m [G], l [G]
+  float* part;
   int32_t slot_floats;
-  // 1: split heads only publish partials and reduce_kernel merges them;
-  // 0: the last warp to finish a split head merges it (atomic ticket).
-  int32_t merge_in_kernel;
   // cross-device state output (optional)
   float* state_o;
   float* state_lse;
@@ -89,6 +104,22 @@ struct DecodeParams {
 // [floor(w*T/W), floor((w+1)*T/W)).
 __device__ __forceinline__ int warp_of_page(int64_t P, int64_t T, int W) {
   return static_cast<int>(((P + 1) * W - 1) / T);
+}
+
+// Segment of global page P: warp w's range is a static prefix (segment
+// w*(m+1)) followed by m chunks of K pages (segments w*(m+1) + 1 .. m).  The
+// pages of a head that fall in one segment form one unit of work and one
+// partial state (unless the head lies wholly in the segment); heads and
+// segments are both ordered by page, so slot head + segment is unique and a
+// head's partials fill slots [head + seg(first page), head + seg(last page)].
+// Which warp computes a segment is decided at run time, but the segments,
+// their partial states and the merge order are not: results do not depend
+// on the schedule.
+__device__ __forceinline__ int segment_of_page(int P, int T, int W, int m, int K) {
+  const int w = warp_of_page(P, T, W);
+  if (m == 0) return w;
+  const int t = static_cast<int>(static_cast<int64_t>(w + 1) * T / W) - m * K;
+  return w * (m + 1) + (P < t ? 0 : 1 + (P - t) / K);
 }
 
 template <typename T>
@@ -133,7 +164,6 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
         L = cap;
       }
       pages = (L + p.bs - 1) / p.bs;
-      p.tickets[hd] = 0u;
     }
     int x = pages;  // inclusive scan within the warp
 #pragma unroll
@@ -168,7 +198,30 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   // include them; capping W at the page count gives every warp >= 1 page.
   const int64_t total = carry;
   const int W = static_cast<int>(total < p.total_warps ? total : p.total_warps);
-  if (tid == 0) *p.weff = W;
+  // Dynamic tail: about a quarter of every range, in at most steal_m_max
+  // chunks of whole stages; none when ranges are shorter than four stages.
+  int sm_m = 0, sm_k = 0;
+  if (W > 1 && p.steal_m_max > 0) {
+    const int ppw = static_cast<int>(total / W);
+    const int tail = ppw / 4;
+    const int pps = p.steal_pps;
+    if (tail >= pps) {
+      const int per = (tail + p.steal_m_max - 1) / p.steal_m_max;
+      sm_k = (per + pps - 1) / pps * pps;
+      sm_m = tail / sm_k;
+      if (sm_m > p.steal_m_max) sm_m = p.steal_m_max;
+      if (sm_m == 0) sm_k = 0;
+    }
+  }
+  if (tid == 0) {
+    *p.weff = W;
+    p.steal[0] = sm_m;
+    p.steal[1] = sm_k;
+    p.steal[2] = sm_m * W;  // chunks left to claim
+    p.steal[3] = 0;         // thief cursor
+  }
+  if (sm_m > 0)
+    for (int w = tid; w < W; w += 1024) p.claims[w] = 0ull;
   for (int hd = tid; hd < n_heads; hd += 1024) {
     const int64_t c0 = p.cum[hd], c1 = p.cum[hd + 1];
     if (c1 > c0) {
@@ -190,68 +243,6 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
         } else {
           T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh;
           for (int d = 0; d < p.D; ++d) o[d] = from_float<T>(0.f);
-        }
-      }
-    }
-  }
-}
-
-// --------------------------------------------------------------------------
-// Merge helpers.  (m, l) pairs are running maxima (log2 units) and sums of
-// 2^(score - m); combining folds the second pair into the first.  An empty
-// pair has m = -inf, l = 0.
-__device__ __forceinline__ void sm_combine(float& m, float& l, float m2, float l2) {
-  const float mn = fmaxf(m, m2);
-  if (mn == -INFINITY) return;  // both empty
-  l = l * fast_exp2(m - mn) + l2 * fast_exp2(m2 - mn);
-  m = mn;
-}
-
-// acc[k] = sum over spans j of 2^(m_j[g] - M[g]) * acc_j[g][d..d+3] for K of
-// this lane's float4 output elements, e = lane + 32 * (k0 + k) (g = 4e / D,
-// d = 4e % D), loading SB spans x K elements per batch so that 16 loads are
-// in flight.  M[g] is read from scratch[g].  Elements past the output
-// (e >= G*D/4) read slot offset 0 and are not stored by the caller.
-template <int K>
-__device__ __forceinline__ void merge_accumulate(const float* base, int sf, int nspans, int G,
-                                                 int D, int lane, int k0, const float* scratch,
-                                                 float4 (&acc)[K]) {
-  constexpr int SB = 16 / K;
-  const int e4 = G * D / 4;
-  int off[K], goff[K];
-  float Mg[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int e = lane + 32 * (k0 + k);
-    const int g = e < e4 ? (e * 4) / D : 0;
-    off[k] = e < e4 ? e * 4 : 0;  // g*D + d == 4e
-    goff[k] = G * D + g;
-    Mg[k] = scratch[g];
-    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  for (int j0 = 0; j0 < nspans; j0 += SB) {
-    float4 v[SB][K];
-    float mm[SB][K];
-#pragma unroll
-    for (int b = 0; b < SB; ++b) {
-      const int j = j0 + b < nspans ? j0 + b : nspans - 1;
-      const float* ps = base + static_cast<int64_t>(j) * sf;
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        v[b][k] = __ldcg(reinterpret_cast<const float4*>(ps + off[k]));
-        mm[b][k] = __ldcg(ps + goff[k]);
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < SB; ++b) {
-      if (j0 + b < nspans) {
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-          const float w = fast_exp2(mm[b][k] - Mg[k]);
-          acc[k].x += w * v[b][k].x;
-          acc[k].y += w * v[b][k].y;
-          acc[k].z += w * v[b][k].z;
-          acc[k].w += w * v[b][k].w;
         }
       }
     }
@@ -343,20 +334,32 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int wpc = blockDim.x >> 5;
   const int depth = p.depth;
   const int gw = blockIdx.x * wpc + warp;
-  // Everything below reads what the planner wrote.  The three start-up
-  // values are independent loads, issued together (wstart has total_warps
-  // entries, so the read is in bounds even for a warp that then exits).
+  // Everything below reads what the planner wrote.  The start-up values are
+  // independent loads, issued together (wstart has total_warps entries, so
+  // the read is in bounds even for a warp that then exits).
   grid_dependency_wait();
   const int n_heads = p.B * p.Hkv;
   const int W = *p.weff;  // min(total_warps, total pages), set by the planner
   // Total pages < 2^31 (checked on the host), so page indices are 32-bit.
   const int total = p.cum[n_heads];
   const int first_head = gw < p.total_warps ? p.wstart[gw] : 0;
+  const int4 steal = *reinterpret_cast<const int4*>(p.steal);
   if (gw >= W) return;
   if (total == 0) return;
+  const int sm_m = steal.x, sm_k = steal.y;
+  // reduce_kernel may be scheduled now; it waits for this grid to complete.
+  grid_launch_dependents();
   const int gs = static_cast<int>(static_cast<int64_t>(gw) * total / W);
-  const int ge = static_cast<int>(static_cast<int64_t>(gw + 1) * total / W);
-  if (gs >= ge) return;
+  const int g_end = static_cast<int>(static_cast<int64_t>(gw + 1) * total / W);
+  if (gs >= g_end) return;
+  // Current segment [c_gp, ge): the static prefix first, then tail chunks
+  // claimed from the front of this warp's tail, then chunks stolen from the
+  // back of other warps' tails.  run_start is the segment's first page.
+  int ge = g_end - sm_m * sm_k;
+  int run_start = gs;
+  int mode = 0;  // 0: own range, 1: stealing, 2: no work left
+  unsigned long long pend = 0ull;  // lane 0: result of the owner's claim
+  bool claim_sent = false;
 
   const int G = p.G, Hkv = p.Hkv, bs = p.bs;
   const int log2_bs = __ffs(bs) - 1;          // bs is a power of two
@@ -401,8 +404,9 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     }
     win_len = L;
   };
+  int c_gp = gs;  // next global page to stage
   // Current head of the issue cursor and what the stages of it need.
-  int c_head = 0, c_h = 0, c_lo = 0, c_hi = 0, c_len = 0, c_nspans = 0, c_wfirst = 0;
+  int c_head = 0, c_h = 0, c_lo = 0, c_hi = 0, c_len = 0, c_slot = 0, c_vfirst = 0, c_vlast = 0;
   const int32_t* c_bt = p.bt;
   int64_t c_pid_add = 0;
   auto enter_head = [&](int hd) {
@@ -416,21 +420,113 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       c_h = hd - s * Hkv;
       c_bt = p.bt + s * p.bt_sb + c_h * p.bt_sh;
       c_pid_add = static_cast<int64_t>(c_h) * p.bt_add;
-      c_wfirst = warp_of_page(c_lo, total, W);
-      c_nspans = warp_of_page(c_hi - 1, total, W) - c_wfirst + 1;
+      c_vfirst = segment_of_page(c_lo, total, W, sm_m, sm_k);
+      c_vlast = segment_of_page(c_hi - 1, total, W, sm_m, sm_k);
+      c_slot = segment_of_page(c_lo > run_start ? c_lo : run_start, total, W, sm_m, sm_k);
     }
   };
   load_window(first_head);
   enter_head(win);
 
-  int c_gp = gs;  // next global page to stage
+  // Largest head hd with cum[hd] <= P (the head holding global page P):
+  // 32 probes per round narrow the range 32-fold.
+  auto find_head = [&](int P) -> int {
+    int lo = 0, hi = n_heads;
+    while (hi - lo > 1) {
+      const int step = (hi - lo + 31) / 32;
+      const int x = lo + lane * step;
+      const bool le = x < hi && p.cum[x] <= P;  // true for lane 0: cum[lo] <= P
+      const unsigned mask = __ballot_sync(0xffffffffu, le);
+      lo += (31 - __clz(mask)) * step;
+      hi = lo + step < hi ? lo + step : hi;
+    }
+    return lo;
+  };
+  // Claim a tail chunk of another warp (from the back of its tail).  Each
+  // round reads the claim words of 32 warps picked by a shared cursor and
+  // tries the one with the most chunks left; gives up once the planner's
+  // count of unclaimed chunks reaches zero or after a bounded number of
+  // rounds.  Returns the chunk's first page, or -1.
+  auto steal_chunk = [&]() -> int {
+    const int rounds = 2 * ((W + 31) / 32) + 2;
+    for (int r = 0; r < rounds; ++r) {
+      int left = 0;
+      uint32_t c0 = 0;
+      if (lane == 0) {
+        left = *reinterpret_cast<volatile int32_t*>(p.steal + 2);
+        c0 = atomicAdd(reinterpret_cast<unsigned int*>(p.steal + 3), 32u);
+      }
+      left = __shfl_sync(0xffffffffu, left, 0);
+      if (left <= 0) return -1;
+      c0 = __shfl_sync(0xffffffffu, c0, 0);
+      const int v = static_cast<int>((c0 + lane) % static_cast<uint32_t>(W));
+      const unsigned long long wd =
+          *reinterpret_cast<volatile unsigned long long*>(p.claims + v);
+      const int used = static_cast<int>(static_cast<uint32_t>(wd)) +
+                       static_cast<int>(static_cast<uint32_t>(wd >> 32));
+      const int rem = used < sm_m ? sm_m - used : 0;
+      int key = (rem << 5) | (31 - lane);  // most left, then lowest lane
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+      if ((key >> 5) == 0) continue;
+      const int vb = __shfl_sync(0xffffffffu, v, 31 - (key & 31));
+      unsigned long long old = 0ull;
+      if (lane == 0) old = atomicAdd(p.claims + vb, 1ull << 32);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      const uint32_t f = static_cast<uint32_t>(old), b = static_cast<uint32_t>(old >> 32);
+      if (f + b < static_cast<uint32_t>(sm_m)) {
+        if (lane == 0) atomicSub(p.steal + 2, 1);
+        const int a1 = static_cast<int>(static_cast<int64_t>(vb + 1) * total / W);
+        return a1 - static_cast<int>(b + 1) * sm_k;  // chunk m - b (1-based)
+      }
+    }
+    return -1;
+  };
+  // The current segment is used up: move to this warp's next tail chunk
+  // (which starts where the segment ended) or to a stolen one.  The owner's
+  // claim is sent with the segment's last stage, not earlier, so that a slow
+  // warp keeps no chunk reserved that a faster one could take.
+  auto next_region = [&]() -> bool {
+    if (mode == 0) {
+      if (sm_m > 0) {
+        if (!claim_sent && lane == 0) pend = atomicAdd(p.claims + gw, 1ull);
+        claim_sent = false;
+        const unsigned long long old = __shfl_sync(0xffffffffu, pend, 0);
+        const uint32_t f = static_cast<uint32_t>(old), b = static_cast<uint32_t>(old >> 32);
+        if (f + b < static_cast<uint32_t>(sm_m)) {
+          run_start = ge;  // chunk f + 1
+          ge += sm_k;
+          if (c_gp < c_hi)
+            c_slot = segment_of_page(run_start, total, W, sm_m, sm_k);
+          if (lane == 0) atomicSub(p.steal + 2, 1);
+          return true;
+        }
+      }
+      mode = 1;
+    }
+    if (mode == 1) {
+      const int cs = sm_m > 0 ? steal_chunk() : -1;
+      if (cs >= 0) {
+        c_gp = cs;
+        ge = cs + sm_k;
+        run_start = cs;
+        const int hd = find_head(cs);
+        load_window(hd);
+        enter_head(hd);
+        return true;
+      }
+      mode = 2;
+    }
+    return false;
+  };
+
   // Next stage, prepared one issue ahead so its block-table loads overlap.
   bool nx_valid = false;
-  int nx_head = 0, nx_h = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_nspans = 0,
-      nx_wfirst = 0;
+  int nx_head = 0, nx_h = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_slot = 0, nx_vfirst = 0,
+      nx_vlast = 0;
   int64_t nx_pid = 0;  // lane i < nx_np: page id of page i of the stage
   auto prepare_next = [&]() {
-    if (c_gp >= ge) {
+    if (c_gp >= ge && !next_region()) {
       nx_valid = false;
       return;
     }
@@ -443,9 +539,16 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     if (c_hi - c_gp < np) np = c_hi - c_gp;
     if (ge - c_gp < np) np = ge - c_gp;
     nx_np = np;
+    // The segment's last stage: claim this warp's next tail chunk now, so the
+    // atomic completes while the stages in flight are computed.
+    if (mode == 0 && sm_m > 0 && !claim_sent && c_gp + np >= ge) {
+      if (lane == 0) pend = atomicAdd(p.claims + gw, 1ull);
+      claim_sent = true;
+    }
     nx_len = c_len;
-    nx_nspans = c_nspans;
-    nx_wfirst = c_wfirst;
+    nx_slot = c_slot;
+    nx_vfirst = c_vfirst;
+    nx_vlast = c_vlast;
     if (lane < np)
       nx_pid = static_cast<int64_t>(c_bt[static_cast<int64_t>(nx_lp0 + lane) * p.bt_si]) *
                    p.bt_mul + c_pid_add;
@@ -456,7 +559,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     const uint32_t bar = bars + slot * 8;
     if (lane == 0) {
       meta[slot * 2] = make_int4(nx_head, nx_lp0, nx_np, nx_len);
-      meta[slot * 2 + 1] = make_int4(nx_nspans, nx_wfirst, 0, 0);
+      meta[slot * 2 + 1] = make_int4(nx_slot, 0, nx_vfirst, nx_vlast);
       mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nx_np << (log2_bs + LOG2_NH + 8)));
     }
     __syncwarp();
@@ -499,16 +602,20 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   float cacc[kCoreMaxG][DL];
   float cm[kCoreMaxG], cl[kCoreMaxG];
 
-  auto start_head = [&](int hd) {
+  // Resets the running state for a new segment of head `hd`; loads the
+  // head's query group unless it is already in place (same head).
+  auto start_head = [&](int hd, bool load_q) {
     const int s = hd / Hkv, h = hd - s * Hkv;
     const T* qp = static_cast<const T*>(p.q) + s * p.q_sb + static_cast<int64_t>(h) * G * p.q_sh;
     if constexpr (CORE) {
-      __syncwarp();  // the previous head's q is no longer read
-      for (int idx = lane; idx < kCoreMaxG * D; idx += 32) {
-        const int g = idx / D, d = idx - g * D;
-        qsm[idx] = g < G ? static_cast<float>(qp[g * p.q_sh + d]) : 0.f;
+      if (load_q) {
+        __syncwarp();  // the previous head's q is no longer read
+        for (int idx = lane; idx < kCoreMaxG * D; idx += 32) {
+          const int g = idx / D, d = idx - g * D;
+          qsm[idx] = g < G ? static_cast<float>(qp[g * p.q_sh + d]) : 0.f;
+        }
+        __syncwarp();
       }
-      __syncwarp();
 #pragma unroll
       for (int g = 0; g < kCoreMaxG; ++g) {
         cm[g] = -INFINITY;
@@ -521,16 +628,18 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int g = nt * 8 + lr;
+      if (load_q) {
 #pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        uint32_t b0 = 0, b1 = 0;
-        if (g < G) {
-          const T* row = qp + g * p.q_sh + ks * 16 + lc * 2;
-          b0 = *reinterpret_cast<const uint32_t*>(row);
-          b1 = *reinterpret_cast<const uint32_t*>(row + 8);
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t b0 = 0, b1 = 0;
+          if (g < G) {
+            const T* row = qp + g * p.q_sh + ks * 16 + lc * 2;
+            b0 = *reinterpret_cast<const uint32_t*>(row);
+            b1 = *reinterpret_cast<const uint32_t*>(row + 8);
+          }
+          qb[ks][nt][0] = b0;
+          qb[ks][nt][1] = b1;
         }
-        qb[ks][nt][0] = b0;
-        qb[ks][nt][1] = b1;
       }
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -544,96 +653,12 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     }
   };
 
-  // Merge the partial states of head `hd` written by warps
-  // [wfirst, wfirst + nspans) into its output (last arriver only).  The merge
-  // sits on the critical path of the head's last warp, so both passes keep
-  // many loads in flight: pass 1 strides the lanes over the spans and
-  // combines (max, sum) pairs across lanes; pass 2 accumulates each lane's
-  // output elements over batches of spans loaded together.
-  auto merge_head = [&](int hd, int nspans, int wfirst) {
-    const int s = hd / Hkv, h = hd - s * Hkv;
-    const int Hq = Hkv * G;
-    const int sf = p.slot_floats;
-    const float* base = p.part + static_cast<int64_t>(hd + wfirst) * sf;
-    for (int g0 = 0; g0 < G; g0 += 8) {
-      float mx[8], sm[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        mx[i] = -INFINITY;
-        sm[i] = 0.f;
-      }
-      for (int j = lane; j < nspans; j += 32) {
-        const float* ps = base + static_cast<int64_t>(j) * sf + G * D;
-        float mj[8], lj[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          mj[i] = g0 + i < G ? __ldcg(ps + g0 + i) : -INFINITY;
-          lj[i] = g0 + i < G ? __ldcg(ps + G + g0 + i) : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) sm_combine(mx[i], sm[i], mj[i], lj[i]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float om = __shfl_xor_sync(0xffffffffu, mx[i], o);
-          const float os = __shfl_xor_sync(0xffffffffu, sm[i], o);
-          sm_combine(mx[i], sm[i], om, os);
-        }
-      if (lane == 0) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (g0 + i < G) {
-            scratch[g0 + i] = mx[i];
-            scratch[GP + g0 + i] = sm[i];
-          }
-      }
-    }
-    __syncwarp();
-    const int e4 = G * D / 4;
-    const int per_lane = (e4 + 31) / 32;  // float4 output elements per lane
-    auto emit = [&](int e, const float4& a) {
-      if (e >= e4) return;
-      const int g = (e * 4) / D, d = (e * 4) - g * D;
-      const float inv = 1.f / scratch[GP + g];
-      const int qh = h * G + g;
-      if (p.state_o) {
-        float4 o = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
-        *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + d) = o;
-      } else {
-        T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + d;
-        const uint32_t lo = pack2<T>(a.x * inv, a.y * inv);
-        const uint32_t hi = pack2<T>(a.z * inv, a.w * inv);
-        *reinterpret_cast<uint2*>(o) = make_uint2(lo, hi);
-      }
-    };
-    if (per_lane == 1) {
-      float4 a1[1];
-      merge_accumulate<1>(base, sf, nspans, G, D, lane, 0, scratch, a1);
-      emit(lane, a1[0]);
-    } else if (per_lane == 2) {
-      float4 a2[2];
-      merge_accumulate<2>(base, sf, nspans, G, D, lane, 0, scratch, a2);
-      emit(lane, a2[0]);
-      emit(lane + 32, a2[1]);
-    } else {
-      for (int k0 = 0; k0 < per_lane; k0 += 4) {
-        float4 a4[4];
-        merge_accumulate<4>(base, sf, nspans, G, D, lane, k0, scratch, a4);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) emit(lane + 32 * (k0 + k), a4[k]);
-      }
-    }
-    if (p.state_o) {
-      for (int g = lane; g < G; g += 32)
-        p.state_lse[static_cast<int64_t>(s) * Hq + h * G + g] =
-            (scratch[g] + __log2f(scratch[GP + g])) * kLn2;
-    }
-    __syncwarp();
-  };
-
-  auto finish_head = [&](int hd, int nspans, int wfirst) {
+  // Ends the accumulation of head `hd` in segment `slot`: a head wholly
+  // inside one segment (vfirst == vlast) is written directly; otherwise the
+  // segment's part becomes the partial state in slot hd + `slot` (plain
+  // stores: reduce_kernel merges the head's slots after this grid).
+  auto finish_head = [&](int hd, int slot, int vfirst, int vlast) {
+    const bool whole = vfirst == vlast;
     if constexpr (CORE) {
       const int s = hd / Hkv, h = hd - s * Hkv;
       const int Hq = Hkv * G;
@@ -646,7 +671,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
         lt[g] = l;
       }
       const int d0 = lane * DL;
-      if (nspans == 1) {
+      if (whole) {
 #pragma unroll
         for (int g = 0; g < kCoreMaxG; ++g) {
           if (g >= G) break;
@@ -667,7 +692,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
         }
         return;
       }
-      float* ps = p.part + static_cast<int64_t>(hd + gw) * p.slot_floats;
+      float* ps = p.part + static_cast<int64_t>(hd + slot) * p.slot_floats;
 #pragma unroll
       for (int g = 0; g < kCoreMaxG; ++g) {
         if (g >= G) break;
@@ -692,7 +717,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       }
     const int s = hd / Hkv, h = hd - s * Hkv;
     const int Hq = Hkv * G;
-    if (nspans == 1) {
+    if (whole) {
       float inv[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -728,8 +753,8 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       }
       return;
     }
-    // Split head: publish this warp's partial, then take a ticket.
-    float* ps = p.part + static_cast<int64_t>(hd + gw) * p.slot_floats;
+    // Split head: publish this segment's partial.
+    float* ps = p.part + static_cast<int64_t>(hd + slot) * p.slot_floats;
 #pragma unroll
     for (int dt = 0; dt < KS; ++dt)
 #pragma unroll
@@ -753,16 +778,6 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
         }
     }
     }  // CORE / MMA partial publication
-    if (p.merge_in_kernel) return;  // reduce_kernel merges after this kernel
-    __threadfence();
-    __syncwarp();
-    uint32_t ticket = 0;
-    if (lane == 0) ticket = atomicAdd(p.tickets + hd, 1u);
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
-    if (ticket == static_cast<uint32_t>(nspans - 1)) {
-      __threadfence();
-      merge_head(hd, nspans, wfirst);
-    }
   };
 
   // ------------------------------------------------ pipeline
@@ -773,17 +788,20 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     ++issued;
   }
 
-  int cur_head = -1, cur_nspans = 0, cur_wfirst = 0;
+  // Accumulation in progress: head, segment, the head's segment range.
+  int cur_head = -1, cur_slot = -1, cur_vfirst = 0, cur_vlast = 0;
   for (int it = 0; it < issued; ++it) {
     const int slot = it % depth;
     const int4 m0 = meta[slot * 2];
     const int4 m1 = meta[slot * 2 + 1];
-    if (m0.x != cur_head) {
-      if (cur_head >= 0) finish_head(cur_head, cur_nspans, cur_wfirst);
+    if (m0.x != cur_head || m1.x != cur_slot) {
+      if (cur_head >= 0) finish_head(cur_head, cur_slot, cur_vfirst, cur_vlast);
+      const bool new_head = m0.x != cur_head;
       cur_head = m0.x;
-      cur_nspans = m1.x;
-      cur_wfirst = m1.y;
-      start_head(cur_head);
+      cur_slot = m1.x;
+      cur_vfirst = m1.z;
+      cur_vlast = m1.w;
+      start_head(cur_head, new_head);
     }
     const uint32_t bar = bars + slot * 8;
     if (!mbar_wait(bar, static_cast<uint32_t>((it / depth) & 1), kWaitLimitNs)) {
@@ -1005,106 +1023,134 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     }
     if (issue(slot)) ++issued;
   }
-  if (cur_head >= 0) finish_head(cur_head, cur_nspans, cur_wfirst);
+  if (cur_head >= 0) finish_head(cur_head, cur_slot, cur_vfirst, cur_vlast);
 }
 
 // --------------------------------------------------------------------------
 // Reduce kernel: merges the partial states of every split head after the
-// decode kernel (the reduce of src/kernel_triton.py:120-174, planned on the
-// device).  One warp per output row (head, query head g): lanes stride over
-// the head's spans to form (max, sum), the per-span weights are kept in
-// registers and broadcast by shuffle, and each lane accumulates 4 head-dim
-// elements over batches of spans loaded together.
+// decode grid (the reduce of src/kernel_triton.py:120-174, planned on the
+// device).  One CTA of 8 warps per head: warp w folds spans [w*n/8,
+// (w+1)*n/8) of the head's n partial states into a running (max, sum, acc)
+// in one pass (two spans' loads in flight per step), then the 8 warp states
+// are combined in a fixed order through shared memory, so the result does not
+// depend on timing.  Lane l owns the float4 output elements f = l + 32 k
+// (query head g = 4f / D).  Shared memory: 8 * (G*D + 2*G) floats.
+__host__ __device__ constexpr int reduce_smem_floats(int G, int D) { return 8 * (G * D + 2 * G); }
+
 template <typename T>
 __global__ void __launch_bounds__(256) reduce_kernel(const DecodeParams p) {
-  const int lane = threadIdx.x & 31;
-  const int G = p.G, D = p.D;
+  extern __shared__ float red[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.G, D = p.D, GD = G * D;
   const int n_heads = p.B * p.Hkv;
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);  // hd * G + g
+  const int hd = blockIdx.x;
   grid_dependency_wait();  // partials written by the decode grid
-  if (row >= n_heads * G) return;
-  const int hd = row / G, g = row - hd * G;
   const int c0 = p.cum[hd], c1 = p.cum[hd + 1];
-  if (c1 <= c0) return;  // empty head: written by the planner
   const int W = *p.weff;
   const int total = p.cum[n_heads];
-  const int wfirst = warp_of_page(c0, total, W);
-  const int nspans = warp_of_page(c1 - 1, total, W) - wfirst + 1;
-  if (nspans == 1) return;  // written by the decode kernel
+  const int sm_m = p.steal[0], sm_k = p.steal[1];
+  if (c1 <= c0) return;  // empty head: written by the planner
+  const int vfirst = segment_of_page(c0, total, W, sm_m, sm_k);
+  const int nspans = segment_of_page(c1 - 1, total, W, sm_m, sm_k) - vfirst + 1;
+  if (nspans == 1) return;  // one segment: written by the decode kernel
   const int sf = p.slot_floats;
-  const float* base = p.part + static_cast<int64_t>(hd + wfirst) * sf;
-  // Spans j = lane + 32 r, r < 4, are this lane's; more than 128 spans per
-  // head fall back to reloading m from memory in the accumulation.
-  float mj[4], mx = -INFINITY, sm = 0.f;
+  const float* base = p.part + static_cast<int64_t>(hd + vfirst) * sf;
+  const int j0 = static_cast<int>(static_cast<int64_t>(warp) * nspans / 8);
+  const int j1 = static_cast<int>(static_cast<int64_t>(warp + 1) * nspans / 8);
+  const int nf = GD / 4;
+  float* wacc = red + warp * GD;           // [8][G*D]
+  float* wmax = red + 8 * GD;              // [8][G]
+  float* wsum = red + 8 * GD + 8 * G;      // [8][G]
+  for (int f0 = lane; f0 < nf; f0 += 128) {
+    float4 a[4];
+    float M[4], L[4];
+    int gk[4];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int j = lane + 32 * r;
-    mj[r] = -INFINITY;
-    if (j < nspans) {
-      const float* ps = base + static_cast<int64_t>(j) * sf + G * D;
-      mj[r] = __ldcg(ps + g);
-      sm_combine(mx, sm, mj[r], __ldcg(ps + G + g));
+    for (int k = 0; k < 4; ++k) {
+      a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      M[k] = -INFINITY;
+      L[k] = 0.f;
+      const int f = f0 + 32 * k;
+      gk[k] = f < nf ? (4 * f) / D : 0;
     }
-  }
-  for (int j = lane + 128; j < nspans; j += 32) {
-    const float* ps = base + static_cast<int64_t>(j) * sf + G * D;
-    sm_combine(mx, sm, __ldcg(ps + g), __ldcg(ps + G + g));
-  }
+#pragma unroll 1
+    for (int j = j0; j < j1; j += 2) {
+      float4 v[2][4];
+      float m[2][4], l[2][4];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-    const float os = __shfl_xor_sync(0xffffffffu, sm, o);
-    sm_combine(mx, sm, om, os);
-  }
-  float wj[4];
+      for (int u = 0; u < 2; ++u) {
+        const int jj = j + u < j1 ? j + u : j;
+        const float* ps = base + static_cast<int64_t>(jj) * sf;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) wj[r] = fast_exp2(mj[r] - mx);
-  const float inv = 1.f / sm;
-  const int Hq = p.Hkv * G;
-  const int s = hd / p.Hkv, h = hd - s * p.Hkv;
-  const int qh = h * G + g;
-  const int iters = (D + 127) / 128;  // the same for every lane (shuffles below)
-  for (int it = 0; it < iters; ++it) {
-    const int c = lane * 4 + it * 128;
-    const bool active = c < D;
-    const int cc = active ? c : 0;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j0 = 0; j0 < nspans; j0 += 16) {
-      float4 v[16];
-#pragma unroll
-      for (int b = 0; b < 16; ++b) {
-        const int j = j0 + b < nspans ? j0 + b : nspans - 1;
-        v[b] = __ldcg(reinterpret_cast<const float4*>(base + static_cast<int64_t>(j) * sf + g * D + cc));
+        for (int k = 0; k < 4; ++k) {
+          const int f = f0 + 32 * k;
+          v[u][k] = f < nf ? __ldcg(reinterpret_cast<const float4*>(ps) + f)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+          m[u][k] = __ldcg(ps + GD + gk[k]);
+          l[u][k] = __ldcg(ps + GD + G + gk[k]);
+        }
       }
 #pragma unroll
-      for (int b = 0; b < 16; ++b) {
-        const int j = j0 + b;
-        const int r = (j >> 5) & 3;  // warp-uniform
-        const float src = r == 0 ? wj[0] : (r == 1 ? wj[1] : (r == 2 ? wj[2] : wj[3]));
-        float w = __shfl_sync(0xffffffffu, src, j & 31);
-        if (j >= 128 && j < nspans)
-          w = fast_exp2(__ldcg(base + static_cast<int64_t>(j) * sf + G * D + g) - mx);
-        if (j < nspans) {
-          a.x += w * v[b].x;
-          a.y += w * v[b].y;
-          a.z += w * v[b].z;
-          a.w += w * v[b].w;
+      for (int u = 0; u < 2; ++u) {
+        if (j + u >= j1) break;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float mn = fmaxf(M[k], m[u][k]);
+          const float sa = fast_exp2(M[k] - mn), sb = fast_exp2(m[u][k] - mn);
+          a[k].x = a[k].x * sa + v[u][k].x * sb;
+          a[k].y = a[k].y * sa + v[u][k].y * sb;
+          a[k].z = a[k].z * sa + v[u][k].z * sb;
+          a[k].w = a[k].w * sa + v[u][k].w * sb;
+          L[k] = L[k] * sa + l[u][k] * sb;
+          M[k] = mn;
         }
       }
     }
-    if (active) {
-      if (p.state_o) {
-        *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + c) =
-            make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
-      } else {
-        T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + c;
-        *reinterpret_cast<uint2*>(o) =
-            make_uint2(pack2<T>(a.x * inv, a.y * inv), pack2<T>(a.z * inv, a.w * inv));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int f = f0 + 32 * k;
+      if (f < nf) {
+        reinterpret_cast<float4*>(wacc)[f] = a[k];
+        if ((4 * f) % D == 0) {  // every lane of query head g holds the same (M, L)
+          wmax[warp * G + gk[k]] = M[k];
+          wsum[warp * G + gk[k]] = L[k];
+        }
       }
     }
   }
-  if (p.state_o && lane == 0)
-    p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (mx + __log2f(sm)) * kLn2;
+  __syncthreads();
+  // Combine the 8 warp states in order and write the head's G outputs.
+  const int Hq = p.Hkv * G;
+  const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+  for (int f = threadIdx.x; f < nf; f += blockDim.x) {
+    const int g = (4 * f) / D, d = 4 * f - g * D;
+    float Mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) Mx = fmaxf(Mx, wmax[w * G + g]);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float sc = fast_exp2(wmax[w * G + g] - Mx);  // empty warp: 2^-inf = 0
+      const float4 x = reinterpret_cast<const float4*>(red + w * GD)[f];
+      o.x += sc * x.x;
+      o.y += sc * x.y;
+      o.z += sc * x.z;
+      o.w += sc * x.w;
+      l += sc * wsum[w * G + g];
+    }
+    const float inv = 1.f / l;
+    const int qh = h * G + g;
+    if (p.state_o) {
+      *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + d) =
+          make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+      if (d == 0) p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (Mx + __log2f(l)) * kLn2;
+    } else {
+      T* out = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + d;
+      *reinterpret_cast<uint2*>(out) =
+          make_uint2(pack2<T>(o.x * inv, o.y * inv), pack2<T>(o.z * inv, o.w * inv));
+    }
+  }
 }
 
 // --------------------------------------------------------------------------

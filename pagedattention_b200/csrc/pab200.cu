@@ -154,12 +154,12 @@ bool select_kernel(int dtype, int D, int nt, int st, bool core, KernelOps* o) {
 struct Plan {
   KernelOps ops;
   int G, nt, st, wpc, depth, ctas_per_sm, grid, W;
-  int merge_in_kernel;
   bool core;
   size_t smem;
   int n_heads;
   int slot_floats;
-  size_t off_cum, off_wstart, off_tickets, off_part, ws_bytes;
+  int steal_m_max;
+  size_t off_cum, off_wstart, off_claims, off_part, ws_bytes;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -338,27 +338,29 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   }
   pl->W = W;
   pl->grid = (W + wpc - 1) / wpc;
-  // Split heads are merged either by their last warp inside the decode kernel
-  // (one warp per head, on the kernel's tail) or by reduce_kernel (one warp
-  // per output row).  The tail merge wins while a head's partials are few
-  // and small; estimate its bytes with every head of equal length.
-  {
-    const double spans = double(W) / pl->n_heads + 1.0;
-    const double merge_bytes = spans * pl->G * D * 4.0;
-    pl->merge_in_kernel = env_int("PAB200_MERGE", merge_bytes > 16384.0 ? 1 : 0) ? 1 : 0;
-  }
-
+  // Partial-state slot: acc [G][D], m [G], l [G].
   pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
-  size_t off = 256;  // status word
-  pl->off_cum = off;
-  off = align256(off + size_t(pl->n_heads + 1) * 4);
-  pl->off_wstart = off;
-  off = align256(off + size_t(W) * 4);
-  pl->off_tickets = off;
-  off = align256(off + size_t(pl->n_heads) * 4);
-  pl->off_part = off;
-  off = align256(off + size_t(pl->n_heads + W) * pl->slot_floats * 4);
-  pl->ws_bytes = off;
+  // Workspace: status, weff and the dynamic-tail header in the first 256
+  // bytes, then cum, wstart, claim words and the partial slots
+  // (n_heads + W * (m_max + 1): one per (head, segment) pair).  The tail
+  // chunk count per warp is capped so that the workspace stays within the
+  // 16 MiB of the no-alloc scratch.
+  int m_max = env_int("PAB200_STEAL_M", 4);
+  if (m_max < 0) m_max = 0;
+  for (;; --m_max) {
+    size_t off = 256;
+    pl->off_cum = off;
+    off = align256(off + size_t(pl->n_heads + 1) * 4);
+    pl->off_wstart = off;
+    off = align256(off + size_t(W) * 4);
+    pl->off_claims = off;
+    off = align256(off + size_t(W) * 8);
+    pl->off_part = off;
+    off = align256(off + (size_t(pl->n_heads) + size_t(W) * (m_max + 1)) * pl->slot_floats * 4);
+    pl->ws_bytes = off;
+    if (m_max == 0 || off <= PAB200_NOALLOC_SCRATCH_BYTES) break;
+  }
+  pl->steal_m_max = m_max;
   return PAB200_OK;
 }
 
@@ -425,8 +427,22 @@ cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s) {
 }
 
 template <typename T>
-cudaError_t launch_reduce(const pab::DecodeParams& p, int rows, cudaStream_t s, bool pdl) {
-  LaunchCfg lc(dim3((rows + 7) / 8), dim3(256), 0, s, pdl);
+cudaError_t launch_reduce(const pab::DecodeParams& p, int n_heads, cudaStream_t s, bool pdl) {
+  const size_t smem = size_t(pab::reduce_smem_floats(p.G, p.D)) * 4;
+  if (smem > 48 * 1024) {
+    // Opt in once per device for the largest query groups (G*D up to 2048).
+    static int done[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+      e = cudaFuncSetAttribute(pab::reduce_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               pab::reduce_smem_floats(32, 64) * 4);
+      if (e != cudaSuccess) return e;
+      done[dev] = 1;
+    }
+  }
+  LaunchCfg lc(dim3(n_heads), dim3(256), smem, s, pdl);
   return cudaLaunchKernelEx(&lc.cfg, pab::reduce_kernel<T>, p);
 }
 
@@ -441,7 +457,7 @@ PAB200_EXPORT size_t pab200_decode_workspace_size(const pab200_decode_args* args
 PAB200_EXPORT int pab200_decode_launch_count(const pab200_decode_args* args) {
   Plan pl;
   if (make_plan(args, &pl) != PAB200_OK) return 0;
-  return pl.merge_in_kernel ? 3 : 2;
+  return 3;
 }
 
 PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
@@ -485,14 +501,16 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   p.depth = pl.depth;
   p.status = reinterpret_cast<uint32_t*>(ws);
   p.weff = reinterpret_cast<int32_t*>(ws + 4);
+  p.steal = reinterpret_cast<int32_t*>(ws + 16);
+  p.claims = reinterpret_cast<unsigned long long*>(ws + pl.off_claims);
+  p.steal_m_max = pl.steal_m_max;
+  p.steal_pps = pl.st / a->block_size;
   p.cum = reinterpret_cast<int32_t*>(ws + pl.off_cum);
   p.wstart = reinterpret_cast<int32_t*>(ws + pl.off_wstart);
-  p.tickets = reinterpret_cast<uint32_t*>(ws + pl.off_tickets);
   p.part = reinterpret_cast<float*>(ws + pl.off_part);
   p.slot_floats = pl.slot_floats;
   p.state_o = a->state_o;
   p.state_lse = a->state_lse;
-  p.merge_in_kernel = pl.merge_in_kernel;
 
   CUtensorMap kmap, vmap;
   if (a->num_pages > 0) {
@@ -520,11 +538,10 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
     e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_after), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  if (pl.merge_in_kernel) {
-    const int rows = pl.n_heads * pl.G;
+  {
     const bool pdl_r = pdl && !a->event_after;
-    e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, rows, s, pdl_r)
-                                      : launch_reduce<__half>(p, rows, s, pdl_r);
+    e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, pl.n_heads, s, pdl_r)
+                                      : launch_reduce<__half>(p, pl.n_heads, s, pdl_r);
     if (e != cudaSuccess) return cuda_fail(e, "reduce kernel launch");
   }
   return PAB200_OK;

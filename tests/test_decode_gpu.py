@@ -92,31 +92,46 @@ def test_known_answers(cuda_device):
     assert torch.count_nonzero(out[0, 0, 4:]) == 0
 
 
-@pytest.mark.parametrize("mode", ["0", "1"])
+@pytest.mark.parametrize("steal_m", ["0", "2", "8"])
 @pytest.mark.parametrize("B,Hkv,G,D,bs,dtype", [(3, 2, 4, 128, 16, torch.bfloat16),
                                                  (2, 1, 32, 64, 8, torch.float16),
                                                  (2, 2, 1, 256, 32, torch.bfloat16)])
-def test_merge_modes_agree(cuda_device, monkeypatch, mode, B, Hkv, G, D, bs, dtype):
-    """Split heads merged by their last warp (PAB200_MERGE=0) or by the
-    separate reduce kernel (PAB200_MERGE=1) give the oracle's result."""
-    monkeypatch.setenv("PAB200_MERGE", mode)
+def test_tail_chunks_agree(cuda_device, monkeypatch, steal_m, B, Hkv, G, D, bs, dtype):
+    """With no tail chunks (PAB200_STEAL_M=0: a static split) or with 2 or 8
+    run-time-claimed chunks per warp range, the merged result is the
+    oracle's."""
+    monkeypatch.setenv("PAB200_STEAL_M", steal_m)
     lens = [[3000 - 700 * h - 300 * s for h in range(Hkv)] for s in range(B)]
     q, k, v, sl, bt, scale = random_case(B, Hkv, G, D, bs, lens, dtype, seed=31)
     dev = cuda_device
     out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
-    assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"merge mode {mode}")
+    assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"tail chunks {steal_m}")
 
 
-@pytest.mark.parametrize("merge", ["0", "1"])
+def test_schedule_independent_results(cuda_device):
+    """Which warp computes a tail chunk is decided at run time, but segments
+    and merge order are fixed: many repeated calls on a batch large enough
+    for every warp to own tail chunks are bit-identical."""
+    lens = [[4096 + 512 * ((s * 3 + h) % 5) for h in range(4)] for s in range(24)]
+    q, k, v, sl, bt, scale = random_case(24, 4, 4, 128, 16, lens, torch.bfloat16, seed=77)
+    dev = cuda_device
+    args = [t.to(dev) for t in (q, k, v, sl, bt)]
+    first = _b200()(*args, scale)
+    for _ in range(20):
+        assert torch.equal(_b200()(*args, scale), first)
+    assert_close(first, run_oracle(q, k, v, sl, bt, scale), what="schedule")
+
+
+@pytest.mark.parametrize("steal_m", ["0", "4"])
 @pytest.mark.parametrize("B,Hkv,G,D,bs,dtype", [(3, 4, 1, 128, 16, torch.float16),
                                                  (2, 2, 2, 128, 32, torch.bfloat16),
                                                  (3, 2, 4, 128, 16, torch.bfloat16),
                                                  (2, 3, 3, 64, 8, torch.float16)])
-def test_cuda_core_path_vs_oracle(cuda_device, monkeypatch, merge, B, Hkv, G, D, bs, dtype):
+def test_cuda_core_path_vs_oracle(cuda_device, monkeypatch, steal_m, B, Hkv, G, D, bs, dtype):
     """The CUDA-core arithmetic variant (PAB200_CORE=1, query groups <= 4)
-    against the oracle, over lengths 0..1000 and both merge modes."""
+    against the oracle, over lengths 0..1000, with and without tail chunks."""
     monkeypatch.setenv("PAB200_CORE", "1")
-    monkeypatch.setenv("PAB200_MERGE", merge)
+    monkeypatch.setenv("PAB200_STEAL_M", steal_m)
     pool = [0, 1, bs - 1, bs, bs + 1, 31, 32, 33, 200, 513, 1000]
     lens = [[pool[(s * Hkv + h * 3) % len(pool)] for h in range(Hkv)] for s in range(B)]
     q, k, v, sl, bt, scale = random_case(B, Hkv, G, D, bs, lens, dtype, seed=G * 10 + B)
