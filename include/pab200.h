@@ -147,9 +147,9 @@ int pab200_decode_launch_count(const pab200_decode_args* args);
 /* Paged-attention decode.  Replaces flash_attn_with_kvcache_wrapper_triton
  * (src/kernel_triton.py:181-307: planner + split kernel + reduce kernel) with
  * launches on `stream`: a device-side planner (no host sync), the split-KV
- * decode kernel and a log-sum-exp reduce kernel for heads split across warps
- * (scheduled early by programmatic dependent launch).  Results do not depend
- * on run-time scheduling: repeated calls are bit-identical.  `workspace` is a device buffer
+ * decode kernel and a log-sum-exp reduce kernel for the heads it split
+ * across warps (scheduled early by programmatic dependent launch).  Results
+ * do not depend on run-time scheduling: repeated calls are bit-identical.  `workspace` is a device buffer
  * of at least pab200_decode_workspace_size() bytes, 256-byte aligned; its
  * contents need no initialisation.  `stream` is a cudaStream_t (0 = legacy
  * default stream). */

@@ -34,9 +34,13 @@
 //                  partials and merge order are fixed by the page counts
 //                  alone, so results do not depend on which warp ran which
 //                  chunk.
-//   reduce_kernel  one CTA per split head merges its partial states (the
-//                  reduce kernel of the reference), scheduled early through
-//                  programmatic dependent launch.
+//   reduce kernels merge the split heads' partials after the decode grid
+//                  (the reduce kernel of the reference): one warp per head
+//                  (lanes over its G x D outputs) or per (head, query head)
+//                  row for large groups, or, when heads have many partials,
+//                  one CTA per row whose warps split the partials.  Both are
+//                  launched early (programmatic dependent launch) and wait
+//                  for the decode grid.
 //
 // Shared-memory stage layout (per warp, per ring slot), ST tokens:
 //   K: [D/64 planes][ST rows][128 bytes], then V with the same shape.
@@ -89,6 +93,7 @@ struct DecodeParams {
   // (pages per chunk), chunks left to claim, thief cursor
   int32_t* steal;
   unsigned long long* claims;  // [W] claim words: low 32 bits front, high back
+  int2* hseg;                  // [n_heads] first segment, segment count (0 if empty)
   int32_t steal_m_max;         // tail chunks per warp the workspace holds
   int32_t steal_pps;           // pages per ring stage (ST / block_size)
   // [(n_heads + W * (steal_m_max + 1)) * slot_floats] partial states, one
@@ -138,65 +143,66 @@ __device__ __forceinline__ __half from_float<__half>(float x) {
 template <typename T>
 __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   __shared__ int32_t warp_tot[32];
-  __shared__ int32_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_heads = p.B * p.Hkv;
   const int cap = p.maxb * p.bs;
   const int Hq = p.Hkv * p.G;
   grid_launch_dependents();  // the decode grid may start its prologue now
-  if (tid == 0) {
-    carry = 0;
-    *p.status = 0u;
-  }
-  __syncthreads();
+  if (tid == 0) *p.status = 0u;
+  // Thread t owns heads [t * per, (t + 1) * per): its page counts are loaded
+  // in one round (up to kPer of them kept in registers), summed, and one
+  // block-wide exclusive scan of the sums gives every head's first page.
+  constexpr int kPer = 8;
+  const int per = (n_heads + 1023) / 1024;
+  const int h0 = tid * per;
+  const int h1 = min(h0 + per, n_heads);
   uint32_t flags = 0;
-  for (int base = 0; base < n_heads; base += 1024) {
-    const int hd = base + tid;
-    int pages = 0;
-    if (hd < n_heads) {
-      const int s = hd / p.Hkv, h = hd - s * p.Hkv;
-      int L = p.lens[s * p.l_sb + h * p.l_sh];
-      if (L < 0) {
-        flags |= kStatusNegative;
-        L = 0;
-      } else if (L > cap) {
-        flags |= kStatusClamp;
-        L = cap;
-      }
-      pages = (L + p.bs - 1) / p.bs;
+  auto head_pages = [&](int hd) {
+    const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+    int L = p.lens[s * p.l_sb + h * p.l_sh];
+    if (L < 0) {
+      flags |= kStatusNegative;
+      L = 0;
+    } else if (L > cap) {
+      flags |= kStatusClamp;
+      L = cap;
     }
-    int x = pages;  // inclusive scan within the warp
+    return (L + p.bs - 1) / p.bs;
+  };
+  int pg[kPer];
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    pg[i] = h0 + i < h1 ? head_pages(h0 + i) : 0;
+    sum += pg[i];
+  }
+  for (int hd = h0 + kPer; hd < h1; ++hd) sum += head_pages(hd);
+  int x = sum;  // inclusive scan within the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int v = warp_tot[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
     }
-    if (lane == 31) warp_tot[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-      int v = warp_tot[lane];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += y;
-      }
-      warp_tot[lane] = v;
-    }
-    __syncthreads();
-    if (hd < n_heads)
-      p.cum[hd] = carry + (warp ? warp_tot[warp - 1] : 0) + x - pages;
-    __syncthreads();
-    if (tid == 0) carry += warp_tot[31];
-    __syncthreads();
+    warp_tot[lane] = v;
   }
-  if (flags) atomicOr(p.status, flags);
-  if (tid == 0) p.cum[n_heads] = carry;
   __syncthreads();
+  const int64_t total = warp_tot[31];
+  int run = (warp ? warp_tot[warp - 1] : 0) + x - sum;  // first page of head h0
+  if (flags) atomicOr(p.status, flags);
+  if (tid == 0) p.cum[n_heads] = static_cast<int>(total);
 
   // With more warps than pages some warps would own no page and the span
   // count of a head (warp_of_page(last) - warp_of_page(first) + 1) would
   // include them; capping W at the page count gives every warp >= 1 page.
-  const int64_t total = carry;
   const int W = static_cast<int>(total < p.total_warps ? total : p.total_warps);
   // Dynamic tail: about a quarter of every range, in at most steal_m_max
   // chunks of whole stages; none when ranges are shorter than four stages.
@@ -206,8 +212,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
     const int tail = ppw / 4;
     const int pps = p.steal_pps;
     if (tail >= pps) {
-      const int per = (tail + p.steal_m_max - 1) / p.steal_m_max;
-      sm_k = (per + pps - 1) / pps * pps;
+      const int each = (tail + p.steal_m_max - 1) / p.steal_m_max;
+      sm_k = (each + pps - 1) / pps * pps;
       sm_m = tail / sm_k;
       if (sm_m > p.steal_m_max) sm_m = p.steal_m_max;
       if (sm_m == 0) sm_k = 0;
@@ -222,14 +228,22 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   }
   if (sm_m > 0)
     for (int w = tid; w < W; w += 1024) p.claims[w] = 0ull;
-  for (int hd = tid; hd < n_heads; hd += 1024) {
-    const int64_t c0 = p.cum[hd], c1 = p.cum[hd + 1];
+  // Per head: its first page, the warps whose range starts in it, its
+  // segment range, or (empty head) its zero output.
+  const int tp = static_cast<int>(total);
+  auto place_head = [&](int hd, int pages) {
+    const int64_t c0 = run, c1 = run + pages;
+    p.cum[hd] = run;
+    run += pages;
     if (c1 > c0) {
       // warps whose first page lies in [c0, c1)
       const int64_t wa = (c0 * W + total - 1) / total;
       const int64_t wb = (c1 * W + total - 1) / total;
       for (int64_t w = wa; w < wb; ++w) p.wstart[w] = hd;
+      const int v0 = segment_of_page(static_cast<int>(c0), tp, W, sm_m, sm_k);
+      p.hseg[hd] = make_int2(v0, segment_of_page(static_cast<int>(c1) - 1, tp, W, sm_m, sm_k) - v0 + 1);
     } else {
+      p.hseg[hd] = make_int2(0, 0);
       // Empty head: its output is zero (an empty state in state mode),
       // matching softmax over zero keys times an empty V in
       // src/kernel_eager.py:51-53.
@@ -246,7 +260,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
         }
       }
     }
-  }
+  };
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    if (h0 + i < h1) place_head(h0 + i, pg[i]);
+  for (int hd = h0 + kPer; hd < h1; ++hd) place_head(hd, head_pages(hd));
 }
 
 // --------------------------------------------------------------------------
@@ -300,6 +318,97 @@ __device__ __forceinline__ void load_row_part(uint32_t addr, float (&f)[DL]) {
 }
 
 // --------------------------------------------------------------------------
+// Merge of partial states (the reduce of src/kernel_triton.py:120-174).  A
+// slot holds acc [G][D], m [G] (running max, log2 units) and l [G] (sum of
+// 2^(score - m)); states combine by rescaling to the larger max.
+// One warp folds R query-head rows at once: row r is spans [a[r], b[r])
+// (a < b) of slots base[r] + j * sf, query head g[r].  Batches of SB spans
+// per row are loaded together (each lane its NC float4 head-dim chunks
+// c = 4 lane + 128 i, plus the span's m and l), then folded in span order
+// with an online rescale into (M, L, acc).
+template <int D, int R, int SB>
+__device__ __forceinline__ void fold_rows(const float* const (&base)[R], const int (&g)[R],
+                                          const int (&a)[R], const int (&b)[R], int sf, int G,
+                                          int lane, float (&M)[R], float (&L)[R],
+                                          float4 (&acc)[R][(D + 127) / 128]) {
+  constexpr int NC = (D + 127) / 128;
+  const int GD = G * D;
+  int n = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    M[r] = -INFINITY;
+    L[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) acc[r][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    n = max(n, b[r] - a[r]);
+  }
+  for (int t0 = 0; t0 < n; t0 += SB) {
+    float4 v[R][SB][NC];
+    float mj[R][SB], lj[R][SB];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int u = 0; u < SB; ++u) {
+        const int j = a[r] + t0 + u < b[r] ? a[r] + t0 + u : b[r] - 1;
+        const float* ps = base[r] + static_cast<int64_t>(j) * sf;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const int cc = lane * 4 + 128 * c;
+          v[r][u][c] = cc < D ? __ldcg(reinterpret_cast<const float4*>(ps + g[r] * D + cc))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        mj[r][u] = __ldcg(ps + GD + g[r]);
+        lj[r][u] = __ldcg(ps + GD + G + g[r]);
+      }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int u = 0; u < SB; ++u) {
+        if (a[r] + t0 + u < b[r]) {
+          const float mn = fmaxf(M[r], mj[r][u]);
+          const float sa = fast_exp2(M[r] - mn), sb = fast_exp2(mj[r][u] - mn);
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            acc[r][c].x = acc[r][c].x * sa + v[r][u][c].x * sb;
+            acc[r][c].y = acc[r][c].y * sa + v[r][u][c].y * sb;
+            acc[r][c].z = acc[r][c].z * sa + v[r][u][c].z * sb;
+            acc[r][c].w = acc[r][c].w * sa + v[r][u][c].w * sb;
+          }
+          L[r] = L[r] * sa + lj[r][u] * sb;
+          M[r] = mn;
+        }
+      }
+  }
+}
+
+// Writes a merged row: out (type T) or, in state mode, the fp32 state o and
+// its lse (natural log).  acc holds the lane's chunks c = 4 lane + 128 i.
+template <typename T, int D>
+__device__ __forceinline__ void write_row(const DecodeParams& p, int hd, int g, int lane, float M,
+                                          float L, const float4 (&acc)[(D + 127) / 128]) {
+  const int G = p.G;
+  const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+  const int Hq = p.Hkv * G, qh = h * G + g;
+  const float inv = 1.f / L;
+#pragma unroll
+  for (int i = 0; i < (D + 127) / 128; ++i) {
+    const int c = lane * 4 + 128 * i;
+    if (c >= D) continue;
+    const float4 a = acc[i];
+    if (p.state_o) {
+      *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + c) =
+          make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+    } else {
+      T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + c;
+      *reinterpret_cast<uint2*>(o) =
+          make_uint2(pack2<T>(a.x * inv, a.y * inv), pack2<T>(a.z * inv, a.w * inv));
+    }
+  }
+  if (p.state_o && lane == 0)
+    p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (M + __log2f(L)) * kLn2;
+}
+
+// --------------------------------------------------------------------------
 // Decode kernel.  T: element type; D: head size; NT: query-head tiles of 8
 // (G <= 8*NT); ST: tokens per ring stage (16, 32 or 64; a power of two
 // >= block_size).  CORE selects CUDA-core arithmetic instead of tensor-core
@@ -318,7 +427,6 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   constexpr int PLANE = ST * 128;       // bytes of one plane of one stage
   constexpr int KV_BYTES = NH * PLANE;  // K (or V) bytes per stage
   constexpr int STAGE_BYTES = 2 * KV_BYTES;
-  constexpr int GP = NT * 8;  // padded query-group size
   static_assert(D % 64 == 0 && (ST == 16 || ST == 32 || ST == 64), "shape");
   static_assert(!CORE || (ST == 32 && NT == 1 && D <= 128), "CUDA-core path shape");
   constexpr int DL = D / 32;  // head-dim elements per lane (CUDA-core path)
@@ -344,10 +452,9 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int total = p.cum[n_heads];
   const int first_head = gw < p.total_warps ? p.wstart[gw] : 0;
   const int4 steal = *reinterpret_cast<const int4*>(p.steal);
-  if (gw >= W) return;
-  if (total == 0) return;
+  if (gw >= W || total == 0) return;
   const int sm_m = steal.x, sm_k = steal.y;
-  // reduce_kernel may be scheduled now; it waits for this grid to complete.
+  // The reduce grid may be scheduled now; it waits for this grid to complete.
   grid_launch_dependents();
   const int gs = static_cast<int>(static_cast<int64_t>(gw) * total / W);
   const int g_end = static_cast<int>(static_cast<int64_t>(gw + 1) * total / W);
@@ -371,11 +478,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const uint32_t bars = smem_addr(tail) + warp * kMaxDepth * 8;
   int4* meta = reinterpret_cast<int4*>(tail + wpc * kMaxDepth * 8) +
                warp * kMaxDepth * 2;
-  float* scratch = reinterpret_cast<float*>(
-                       tail + wpc * kMaxDepth * (8 + kMetaBytesPerSlot)) +
-                   warp * 2 * GP;
-  float* qsm = reinterpret_cast<float*>(tail + wpc * kMaxDepth * (8 + kMetaBytesPerSlot) +
-                                        wpc * 2 * GP * 4) +
+  float* qsm = reinterpret_cast<float*>(tail + wpc * kMaxDepth * (8 + kMetaBytesPerSlot)) +
                warp * (core_q_bytes(CORE, D) / 4);
 
   if (lane == 0) {
@@ -1026,131 +1129,173 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   if (cur_head >= 0) finish_head(cur_head, cur_slot, cur_vfirst, cur_vlast);
 }
 
-// --------------------------------------------------------------------------
-// Reduce kernel: merges the partial states of every split head after the
-// decode grid (the reduce of src/kernel_triton.py:120-174, planned on the
-// device).  One CTA of 8 warps per head: warp w folds spans [w*n/8,
-// (w+1)*n/8) of the head's n partial states into a running (max, sum, acc)
-// in one pass (two spans' loads in flight per step), then the 8 warp states
-// are combined in a fixed order through shared memory, so the result does not
-// depend on timing.  Lane l owns the float4 output elements f = l + 32 k
-// (query head g = 4f / D).  Shared memory: 8 * (G*D + 2*G) floats.
-__host__ __device__ constexpr int reduce_smem_floats(int G, int D) { return 8 * (G * D + 2 * G); }
 
-template <typename T>
-__global__ void __launch_bounds__(256) reduce_kernel(const DecodeParams p) {
-  extern __shared__ float red[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int G = p.G, D = p.D, GD = G * D;
+// --------------------------------------------------------------------------
+// Reduce kernels (the reduce of src/kernel_triton.py:120-174, planned on the
+// device).  Row r = (head r / G, query head r % G) of a head whose pages fall
+// in more than one segment folds the head's partial states, slots
+// hd + hseg.x .. hd + hseg.x + hseg.y - 1, in slot order.
+//
+// reduce_heads_kernel: one warp per head, lanes over the head's G x D
+// outputs (float4 f = lane + 32 k, k < NCT; query head g = 4 f / D), so each
+// partial state is read once, coalesced; SB = 16 / NCT partials' loads are
+// in flight per step.  For heads with few partials.  4 warps per CTA.
+template <typename T, int D, int NCT>
+__global__ void __launch_bounds__(128) reduce_heads_kernel(const DecodeParams p) {
+  constexpr int SB = NCT >= 16 ? 1 : 16 / NCT;
+  const int lane = threadIdx.x & 31;
+  const int G = p.G, GD = G * D, nf = GD / 4;
   const int n_heads = p.B * p.Hkv;
-  const int hd = blockIdx.x;
+  const int hd = blockIdx.x * 4 + (threadIdx.x >> 5);
   grid_dependency_wait();  // partials written by the decode grid
-  const int c0 = p.cum[hd], c1 = p.cum[hd + 1];
-  const int W = *p.weff;
-  const int total = p.cum[n_heads];
-  const int sm_m = p.steal[0], sm_k = p.steal[1];
-  if (c1 <= c0) return;  // empty head: written by the planner
-  const int vfirst = segment_of_page(c0, total, W, sm_m, sm_k);
-  const int nspans = segment_of_page(c1 - 1, total, W, sm_m, sm_k) - vfirst + 1;
-  if (nspans == 1) return;  // one segment: written by the decode kernel
+  if (hd >= n_heads) return;
+  const int2 hs = p.hseg[hd];
+  if (hs.y <= 1) return;  // empty, or written whole by the decode kernel
   const int sf = p.slot_floats;
-  const float* base = p.part + static_cast<int64_t>(hd + vfirst) * sf;
-  const int j0 = static_cast<int>(static_cast<int64_t>(warp) * nspans / 8);
-  const int j1 = static_cast<int>(static_cast<int64_t>(warp + 1) * nspans / 8);
-  const int nf = GD / 4;
-  float* wacc = red + warp * GD;           // [8][G*D]
-  float* wmax = red + 8 * GD;              // [8][G]
-  float* wsum = red + 8 * GD + 8 * G;      // [8][G]
-  for (int f0 = lane; f0 < nf; f0 += 128) {
-    float4 a[4];
-    float M[4], L[4];
-    int gk[4];
+  const float* base = p.part + static_cast<int64_t>(hd + hs.x) * sf;
+  int gk[NCT];
+  float M[NCT], L[NCT];
+  float4 acc[NCT];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      M[k] = -INFINITY;
-      L[k] = 0.f;
-      const int f = f0 + 32 * k;
-      gk[k] = f < nf ? (4 * f) / D : 0;
-    }
-#pragma unroll 1
-    for (int j = j0; j < j1; j += 2) {
-      float4 v[2][4];
-      float m[2][4], l[2][4];
+  for (int k = 0; k < NCT; ++k) {
+    const int f = lane + 32 * k;
+    gk[k] = f < nf ? (4 * f) / D : 0;
+    M[k] = -INFINITY;
+    L[k] = 0.f;
+    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int j0 = 0; j0 < hs.y; j0 += SB) {
+    float4 v[SB][NCT];
+    float mj[SB][NCT], lj[SB][NCT];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int jj = j + u < j1 ? j + u : j;
-        const float* ps = base + static_cast<int64_t>(jj) * sf;
+    for (int u = 0; u < SB; ++u) {
+      const int j = j0 + u < hs.y ? j0 + u : hs.y - 1;
+      const float* ps = base + static_cast<int64_t>(j) * sf;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int f = f0 + 32 * k;
-          v[u][k] = f < nf ? __ldcg(reinterpret_cast<const float4*>(ps) + f)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-          m[u][k] = __ldcg(ps + GD + gk[k]);
-          l[u][k] = __ldcg(ps + GD + G + gk[k]);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (j + u >= j1) break;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float mn = fmaxf(M[k], m[u][k]);
-          const float sa = fast_exp2(M[k] - mn), sb = fast_exp2(m[u][k] - mn);
-          a[k].x = a[k].x * sa + v[u][k].x * sb;
-          a[k].y = a[k].y * sa + v[u][k].y * sb;
-          a[k].z = a[k].z * sa + v[u][k].z * sb;
-          a[k].w = a[k].w * sa + v[u][k].w * sb;
-          L[k] = L[k] * sa + l[u][k] * sb;
-          M[k] = mn;
-        }
+      for (int k = 0; k < NCT; ++k) {
+        const int f = lane + 32 * k;
+        v[u][k] = f < nf ? __ldcg(reinterpret_cast<const float4*>(ps) + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+        mj[u][k] = __ldcg(ps + GD + gk[k]);
+        lj[u][k] = __ldcg(ps + GD + G + gk[k]);
       }
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int f = f0 + 32 * k;
-      if (f < nf) {
-        reinterpret_cast<float4*>(wacc)[f] = a[k];
-        if ((4 * f) % D == 0) {  // every lane of query head g holds the same (M, L)
-          wmax[warp * G + gk[k]] = M[k];
-          wsum[warp * G + gk[k]] = L[k];
-        }
+    for (int u = 0; u < SB; ++u) {
+      if (j0 + u >= hs.y) break;
+#pragma unroll
+      for (int k = 0; k < NCT; ++k) {
+        const float mn = fmaxf(M[k], mj[u][k]);
+        const float sa = fast_exp2(M[k] - mn), sb = fast_exp2(mj[u][k] - mn);
+        acc[k].x = acc[k].x * sa + v[u][k].x * sb;
+        acc[k].y = acc[k].y * sa + v[u][k].y * sb;
+        acc[k].z = acc[k].z * sa + v[u][k].z * sb;
+        acc[k].w = acc[k].w * sa + v[u][k].w * sb;
+        L[k] = L[k] * sa + lj[u][k] * sb;
+        M[k] = mn;
       }
     }
   }
-  __syncthreads();
-  // Combine the 8 warp states in order and write the head's G outputs.
   const int Hq = p.Hkv * G;
   const int s = hd / p.Hkv, h = hd - s * p.Hkv;
-  for (int f = threadIdx.x; f < nf; f += blockDim.x) {
-    const int g = (4 * f) / D, d = 4 * f - g * D;
-    float Mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) Mx = fmaxf(Mx, wmax[w * G + g]);
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    float l = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const float sc = fast_exp2(wmax[w * G + g] - Mx);  // empty warp: 2^-inf = 0
-      const float4 x = reinterpret_cast<const float4*>(red + w * GD)[f];
-      o.x += sc * x.x;
-      o.y += sc * x.y;
-      o.z += sc * x.z;
-      o.w += sc * x.w;
-      l += sc * wsum[w * G + g];
-    }
-    const float inv = 1.f / l;
+  for (int k = 0; k < NCT; ++k) {
+    const int f = lane + 32 * k;
+    if (f >= nf) continue;
+    const int g = gk[k], d = 4 * f - g * D;
     const int qh = h * G + g;
+    const float inv = 1.f / L[k];
     if (p.state_o) {
       *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + d) =
-          make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
-      if (d == 0) p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (Mx + __log2f(l)) * kLn2;
+          make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
+      if (d == 0) p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (M[k] + __log2f(L[k])) * kLn2;
     } else {
-      T* out = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + d;
-      *reinterpret_cast<uint2*>(out) =
-          make_uint2(pack2<T>(o.x * inv, o.y * inv), pack2<T>(o.z * inv, o.w * inv));
+      T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + d;
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack2<T>(acc[k].x * inv, acc[k].y * inv),
+                                                pack2<T>(acc[k].z * inv, acc[k].w * inv));
     }
   }
+}
+
+// reduce_rows_kernel: one warp per (head, query head) row, 16 partials'
+// loads in flight per step; for large query groups (G * D > 1024) whose heads
+// hold few partials.  4 warps per CTA.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) reduce_rows_kernel(const DecodeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int G = p.G;
+  const int rows = p.B * p.Hkv * G;
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  grid_dependency_wait();  // partials written by the decode grid
+  if (r >= rows) return;
+  const int hd = r / G, g = r - hd * G;
+  const int2 hs = p.hseg[hd];
+  if (hs.y <= 1) return;  // empty, or written whole by the decode kernel
+  const float* bs1[1] = {p.part + static_cast<int64_t>(hd + hs.x) * p.slot_floats};
+  const int g1[1] = {g}, a1[1] = {0}, b1[1] = {hs.y};
+  float M[1], L[1];
+  float4 acc[1][(D + 127) / 128];
+  fold_rows<D, 1, 16>(bs1, g1, a1, b1, p.slot_floats, G, lane, M, L, acc);
+  write_row<T, D>(p, hd, g, lane, M[0], L[0], acc[0]);
+}
+
+// reduce_split_kernel: one CTA of 4 warps per row; warp w folds partials
+// [w n / 4, (w + 1) n / 4) and the 4 states are combined in order through
+// shared memory; for heads with many partials.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) reduce_split_kernel(const DecodeParams p) {
+  // rows padded to D + 4 floats: every row starts on a 16-byte boundary for
+  // the float4 accesses below; [D] holds M, [D + 1] holds L
+  __shared__ __align__(16) float part_sm[4][D + 4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.G;
+  const int r = blockIdx.x;
+  grid_dependency_wait();  // partials written by the decode grid
+  const int hd = r / G, g = r - hd * G;
+  const int2 hs = p.hseg[hd];
+  if (hs.y <= 1) return;  // uniform across the CTA
+  constexpr int NC = (D + 127) / 128;
+  const int a = static_cast<int>(static_cast<int64_t>(warp) * hs.y / 4);
+  const int b = static_cast<int>(static_cast<int64_t>(warp + 1) * hs.y / 4);
+  float M[1] = {-INFINITY}, L[1] = {0.f};
+  float4 acc[1][NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) acc[0][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (b > a) {
+    const float* bs1[1] = {p.part + static_cast<int64_t>(hd + hs.x) * p.slot_floats};
+    const int g1[1] = {g}, a1[1] = {a}, b1[1] = {b};
+    fold_rows<D, 1, 16>(bs1, g1, a1, b1, p.slot_floats, G, lane, M, L, acc);
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+    if (lane * 4 + 128 * c < D) *reinterpret_cast<float4*>(&part_sm[warp][lane * 4 + 128 * c]) = acc[0][c];
+  if (lane == 0) {
+    part_sm[warp][D] = M[0];
+    part_sm[warp][D + 1] = L[0];
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  float Mx = -INFINITY, Lx = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) Mx = fmaxf(Mx, part_sm[q][D]);
+  float4 o[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) o[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float sc = fast_exp2(part_sm[q][D] - Mx);  // an empty part: 2^-inf = 0
+    Lx += sc * part_sm[q][D + 1];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int cc = lane * 4 + 128 * c;
+      if (cc >= D) continue;
+      const float4 x = *reinterpret_cast<const float4*>(&part_sm[q][cc]);
+      o[c].x += sc * x.x;
+      o[c].y += sc * x.y;
+      o[c].z += sc * x.z;
+      o[c].w += sc * x.w;
+    }
+  }
+  write_row<T, D>(p, hd, g, lane, Mx, Lx, o);
 }
 
 // --------------------------------------------------------------------------

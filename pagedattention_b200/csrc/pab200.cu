@@ -4,9 +4,8 @@
 // (src/kernel_triton.py:181-307).  Differences by design: the chunk plan is
 // computed on the device (no .cpu() sync, no per-call H2D metadata copies,
 // src/kernel_triton.py:206-229), the partial buffers live in a caller-owned
-// workspace (no per-call allocation, :232-243), and split heads are merged
-// inside the split kernel unless their partial states are large, in which
-// case a separate reduce kernel (the reference's own structure) runs.
+// workspace (no per-call allocation, :232-243), and the reduce kernel is
+// scheduled while the decode grid runs (programmatic dependent launch).
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -159,7 +158,7 @@ struct Plan {
   int n_heads;
   int slot_floats;
   int steal_m_max;
-  size_t off_cum, off_wstart, off_claims, off_part, ws_bytes;
+  size_t off_cum, off_wstart, off_claims, off_hseg, off_part, ws_bytes;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -220,7 +219,7 @@ int validate(const pab200_decode_args* a) {
 // mbarriers, stage records and merge scratch (see decode_kernel).
 size_t decode_smem(int wpc, int depth, size_t stage, int nt, int core_bytes) {
   return 1024 + size_t(wpc) * depth * stage +
-         size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + 2 * nt * 8 * 4 + core_bytes);
+         size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + core_bytes);
 }
 
 struct Geometry {
@@ -341,7 +340,8 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   // Partial-state slot: acc [G][D], m [G], l [G].
   pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
   // Workspace: status, weff and the dynamic-tail header in the first 256
-  // bytes, then cum, wstart, claim words and the partial slots
+  // bytes, then cum, wstart, claim words, per-head segment ranges and the
+  // partial slots
   // (n_heads + W * (m_max + 1): one per (head, segment) pair).  The tail
   // chunk count per warp is capped so that the workspace stays within the
   // 16 MiB of the no-alloc scratch.
@@ -355,6 +355,8 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
     off = align256(off + size_t(W) * 4);
     pl->off_claims = off;
     off = align256(off + size_t(W) * 8);
+    pl->off_hseg = off;
+    off = align256(off + size_t(pl->n_heads) * 8);
     pl->off_part = off;
     off = align256(off + (size_t(pl->n_heads) + size_t(W) * (m_max + 1)) * pl->slot_floats * 4);
     pl->ws_bytes = off;
@@ -426,26 +428,51 @@ cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t launch_reduce(const pab::DecodeParams& p, int n_heads, cudaStream_t s, bool pdl) {
-  const size_t smem = size_t(pab::reduce_smem_floats(p.G, p.D)) * 4;
-  if (smem > 48 * 1024) {
-    // Opt in once per device for the largest query groups (G*D up to 2048).
-    static int done[64] = {0};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64 && !done[dev]) {
-      e = cudaFuncSetAttribute(pab::reduce_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               pab::reduce_smem_floats(32, 64) * 4);
-      if (e != cudaSuccess) return e;
-      done[dev] = 1;
-    }
-  }
-  LaunchCfg lc(dim3(n_heads), dim3(256), smem, s, pdl);
-  return cudaLaunchKernelEx(&lc.cfg, pab::reduce_kernel<T>, p);
+
+}  // namespace
+
+namespace {
+// Reduce launch: while heads hold few partial states, one warp per head (or
+// per (head, query head) row when G * D > 1024); when they hold many, one CTA
+// (4 warps splitting the partials) per row.  The expected count assumes
+// equal head lengths.
+template <typename T, int D, int NCT>
+cudaError_t launch_reduce_heads(const pab::DecodeParams& p, int n_heads, cudaStream_t s, bool pdl) {
+  LaunchCfg lc(dim3(static_cast<unsigned>((n_heads + 3) / 4)), dim3(128), 0, s, pdl);
+  return cudaLaunchKernelEx(&lc.cfg, pab::reduce_heads_kernel<T, D, NCT>, p);
 }
 
+template <typename T, int D>
+cudaError_t launch_reduce_d(const pab::DecodeParams& p, const Plan& pl, cudaStream_t s, bool pdl) {
+  const double spans = double(pl.W) * (pl.steal_m_max + 1) / pl.n_heads + 1.0;
+  if (spans <= 24.0) {
+    int nct = 1;  // float4 output chunks per lane: G*D/128 rounded up to a power of two
+    while (nct * 128 < pl.G * D) nct *= 2;
+    switch (nct) {
+      case 1: return launch_reduce_heads<T, D, 1>(p, pl.n_heads, s, pdl);
+      case 2: return launch_reduce_heads<T, D, 2>(p, pl.n_heads, s, pdl);
+      case 4: return launch_reduce_heads<T, D, 4>(p, pl.n_heads, s, pdl);
+      case 8: return launch_reduce_heads<T, D, 8>(p, pl.n_heads, s, pdl);
+      default: {  // G*D > 1024: one warp per (head, query head) row
+        const int64_t rows = int64_t(pl.n_heads) * pl.G;
+        LaunchCfg lc(dim3(static_cast<unsigned>((rows + 3) / 4)), dim3(128), 0, s, pdl);
+        return cudaLaunchKernelEx(&lc.cfg, pab::reduce_rows_kernel<T, D>, p);
+      }
+    }
+  }
+  const int64_t rows = int64_t(pl.n_heads) * pl.G;
+  LaunchCfg lc(dim3(static_cast<unsigned>(rows)), dim3(128), 0, s, pdl);
+  return cudaLaunchKernelEx(&lc.cfg, pab::reduce_split_kernel<T, D>, p);
+}
+
+template <typename T>
+cudaError_t launch_reduce(const pab::DecodeParams& p, const Plan& pl, cudaStream_t s, bool pdl) {
+  switch (p.D) {
+    case 64: return launch_reduce_d<T, 64>(p, pl, s, pdl);
+    case 128: return launch_reduce_d<T, 128>(p, pl, s, pdl);
+    default: return launch_reduce_d<T, 256>(p, pl, s, pdl);
+  }
+}
 }  // namespace
 
 PAB200_EXPORT size_t pab200_decode_workspace_size(const pab200_decode_args* args) {
@@ -503,6 +530,7 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   p.weff = reinterpret_cast<int32_t*>(ws + 4);
   p.steal = reinterpret_cast<int32_t*>(ws + 16);
   p.claims = reinterpret_cast<unsigned long long*>(ws + pl.off_claims);
+  p.hseg = reinterpret_cast<int2*>(ws + pl.off_hseg);
   p.steal_m_max = pl.steal_m_max;
   p.steal_pps = pl.st / a->block_size;
   p.cum = reinterpret_cast<int32_t*>(ws + pl.off_cum);
@@ -538,12 +566,10 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
     e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_after), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  {
-    const bool pdl_r = pdl && !a->event_after;
-    e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, pl.n_heads, s, pdl_r)
-                                      : launch_reduce<__half>(p, pl.n_heads, s, pdl_r);
-    if (e != cudaSuccess) return cuda_fail(e, "reduce kernel launch");
-  }
+  const bool pdl_r = pdl && !a->event_after;
+  e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, pl, s, pdl_r)
+                                    : launch_reduce<__half>(p, pl, s, pdl_r);
+  if (e != cudaSuccess) return cuda_fail(e, "reduce kernel launch");
   return PAB200_OK;
 }
 
