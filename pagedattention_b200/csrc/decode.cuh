@@ -726,8 +726,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
 #pragma unroll
         for (int e = 0; e < DL; ++e) cacc[g][e] = 0.f;
       }
-      return;
-    }
+    } else {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int g = nt * 8 + lr;
@@ -754,12 +753,13 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[dt][nt][i] = 0.f;
     }
+    }  // CORE / MMA state
   };
 
   // Ends the accumulation of head `hd` in segment `slot`: a head wholly
   // inside one segment (vfirst == vlast) is written directly; otherwise the
   // segment's part becomes the partial state in slot hd + `slot` (plain
-  // stores: reduce_kernel merges the head's slots after this grid).
+  // stores: a reduce kernel merges the head's slots after this grid).
   auto finish_head = [&](int hd, int slot, int vfirst, int vlast) {
     const bool whole = vfirst == vlast;
     if constexpr (CORE) {

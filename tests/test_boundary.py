@@ -133,3 +133,30 @@ def test_missing_library_fails_loudly(tmp_path):
     ) % (str(ROOT), str(tmp_path / "missing.so"))
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
     assert "raised" in out.stdout, out.stderr
+
+
+def test_exchange_argument_checks():
+    """Host-side checks of the multi-GPU exchange entry points (no device
+    work): buffer sizing, and refusals before any launch."""
+    lib = _lib.load()
+    assert lib.pab200_exchange_buffer_bytes(0, 8, 128) == 0
+    assert lib.pab200_exchange_buffer_bytes(2, 0, 128) == 0
+    assert lib.pab200_exchange_buffer_bytes(2, 8, 130) == 0
+    rows, D, world = 8, 128, 2
+    S = rows * D + ((rows + 3) // 4) * 4
+    nb = min((rows + 7) // 8, 128)
+    want = 2 * world * S * 8 + ((nb + 3) // 4) * 4 * 4
+    assert lib.pab200_exchange_buffer_bytes(world, rows, D) == want
+    # rank outside [0, world), zero wait limit, null pointers, misalignment
+    args = (16, 16, 2, 2, rows, D, 16, D, _lib.DTYPE_BF16, 10**9, 16, None)
+    assert lib.pab200_exchange_merge(*args) == _lib.ERR_INVALID_ARGUMENT
+    args = (16, 16, 0, 2, rows, D, 16, D, _lib.DTYPE_BF16, 0, 16, None)
+    assert lib.pab200_exchange_merge(*args) == _lib.ERR_INVALID_ARGUMENT
+    args = (None, 16, 0, 2, rows, D, 16, D, _lib.DTYPE_BF16, 10**9, 16, None)
+    assert lib.pab200_exchange_merge(*args) == _lib.ERR_INVALID_ARGUMENT
+    args = (8, 16, 0, 2, rows, D, 16, D, _lib.DTYPE_BF16, 10**9, 16, None)
+    assert lib.pab200_exchange_merge(*args) == _lib.ERR_ALIGNMENT
+    assert lib.pab200_exchange_buffer_close(None) == _lib.OK
+    assert lib.pab200_exchange_buffer_destroy(None) == _lib.OK
+    assert lib.pab200_exchange_buffer_create(0, ctypes.byref(ctypes.c_void_p()), None) == \
+        _lib.ERR_INVALID_ARGUMENT
