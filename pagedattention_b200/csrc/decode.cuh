@@ -93,7 +93,14 @@ struct DecodeParams {
   // (pages per chunk), chunks left to claim, thief cursor
   int32_t* steal;
   unsigned long long* claims;  // [W] claim words: low 32 bits front, high back
-  int2* hseg;                  // [n_heads] first segment, segment count (0 if empty)
+  // [n_heads] first segment and segment count of every head (0 if empty),
+  // for two calls: .xy for parity 0, .zw for parity 1.  The planner of the
+  // next call writes the other half while the reduce of this call still
+  // reads its own, so the two may overlap.
+  int4* hseg;
+  uint32_t* parity;            // which half of hseg the current call uses
+  int32_t* n_empty;            // [1] heads of length 0 in this call
+  int32_t* empty;              // [n_heads] their indices (zeroed by the decode grid)
   int32_t steal_m_max;         // tail chunks per warp the workspace holds
   int32_t steal_pps;           // pages per ring stage (ST / block_size)
   // [(n_heads + W * (steal_m_max + 1)) * slot_floats] partial states, one
@@ -143,12 +150,22 @@ __device__ __forceinline__ __half from_float<__half>(float x) {
 template <typename T>
 __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   __shared__ int32_t warp_tot[32];
+  __shared__ uint32_t par_sm;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_heads = p.B * p.Hkv;
   const int cap = p.maxb * p.bs;
   const int Hq = p.Hkv * p.G;
   grid_launch_dependents();  // the decode grid may start its prologue now
-  if (tid == 0) *p.status = 0u;
+  // This kernel may run while the previous call's reduce kernel drains (it
+  // is launched with programmatic dependent launch and that kernel triggers
+  // once it has read its parity): it writes only state that kernel no longer
+  // reads, the other half of hseg, and waits for it before completing.
+  if (tid == 0) {
+    *p.status = 0u;
+    *p.n_empty = 0;
+    par_sm = (*reinterpret_cast<volatile uint32_t*>(p.parity) ^ 1u) & 1u;
+    *p.parity = par_sm;
+  }
   // Thread t owns heads [t * per, (t + 1) * per): its page counts are loaded
   // in one round (up to kPer of them kept in registers), summed, and one
   // block-wide exclusive scan of the sums gives every head's first page.
@@ -231,6 +248,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   // Per head: its first page, the warps whose range starts in it, its
   // segment range, or (empty head) its zero output.
   const int tp = static_cast<int>(total);
+  const uint32_t par = par_sm;  // set before the scan's barriers
   auto place_head = [&](int hd, int pages) {
     const int64_t c0 = run, c1 = run + pages;
     p.cum[hd] = run;
@@ -241,30 +259,24 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
       const int64_t wb = (c1 * W + total - 1) / total;
       for (int64_t w = wa; w < wb; ++w) p.wstart[w] = hd;
       const int v0 = segment_of_page(static_cast<int>(c0), tp, W, sm_m, sm_k);
-      p.hseg[hd] = make_int2(v0, segment_of_page(static_cast<int>(c1) - 1, tp, W, sm_m, sm_k) - v0 + 1);
+      reinterpret_cast<int2*>(p.hseg + hd)[par] =
+          make_int2(v0, segment_of_page(static_cast<int>(c1) - 1, tp, W, sm_m, sm_k) - v0 + 1);
     } else {
-      p.hseg[hd] = make_int2(0, 0);
-      // Empty head: its output is zero (an empty state in state mode),
-      // matching softmax over zero keys times an empty V in
-      // src/kernel_eager.py:51-53.
-      const int s = hd / p.Hkv, h = hd - s * p.Hkv;
-      for (int g = 0; g < p.G; ++g) {
-        const int qh = h * p.G + g;
-        if (p.state_o) {
-          float* o = p.state_o + (static_cast<int64_t>(s) * Hq + qh) * p.D;
-          for (int d = 0; d < p.D; ++d) o[d] = 0.f;
-          p.state_lse[static_cast<int64_t>(s) * Hq + qh] = -INFINITY;
-        } else {
-          T* o = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh;
-          for (int d = 0; d < p.D; ++d) o[d] = from_float<T>(0.f);
-        }
-      }
+      // Empty head: listed here, its zero output is written by the decode
+      // grid (this kernel may overlap the previous call's reduce, which can
+      // still be writing the same output rows).
+      reinterpret_cast<int2*>(p.hseg + hd)[par] = make_int2(0, 0);
+      p.empty[atomicAdd(p.n_empty, 1)] = hd;
     }
   };
 #pragma unroll
   for (int i = 0; i < kPer; ++i)
     if (h0 + i < h1) place_head(h0 + i, pg[i]);
   for (int hd = h0 + kPer; hd < h1; ++hd) place_head(hd, head_pages(hd));
+  // Complete only after the kernel before this one (the previous call's
+  // reduce): the decode grid that waits for this kernel then cannot
+  // overwrite partial states that reduce still reads.
+  if (tid == 0) grid_dependency_wait();
 }
 
 // --------------------------------------------------------------------------
@@ -452,6 +464,26 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int total = p.cum[n_heads];
   const int first_head = gw < p.total_warps ? p.wstart[gw] : 0;
   const int4 steal = *reinterpret_cast<const int4*>(p.steal);
+  const int n_empty = *p.n_empty;
+  // Heads of length 0 get zeros (an empty state in state mode), matching
+  // softmax over zero keys times an empty V in src/kernel_eager.py:51-53.
+  for (int e = gw; e < n_empty; e += p.total_warps) {
+    const int hd = p.empty[e];
+    const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+    const int Hq = p.Hkv * p.G;
+    for (int g = 0; g < p.G; ++g) {
+      const int qh = h * p.G + g;
+      for (int c = lane * 4; c < D; c += 128) {
+        if (p.state_o)
+          *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + c) =
+              make_float4(0.f, 0.f, 0.f, 0.f);
+        else
+          *reinterpret_cast<uint2*>(static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + c) =
+              make_uint2(0u, 0u);
+      }
+      if (p.state_o && lane == 0) p.state_lse[static_cast<int64_t>(s) * Hq + qh] = -INFINITY;
+    }
+  }
   if (gw >= W || total == 0) return;
   const int sm_m = steal.x, sm_k = steal.y;
   // The reduce grid may be scheduled now; it waits for this grid to complete.
@@ -1130,6 +1162,23 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
 }
 
 
+// Prologue of every reduce kernel: waits for the decode grid, reads the
+// current call's parity in every thread, and only then lets the next call's
+// planner start (it flips the parity and writes the other half of hseg).
+__device__ __forceinline__ uint32_t reduce_prologue(const DecodeParams& p) {
+  grid_dependency_wait();  // partials written by the decode grid
+  const uint32_t par = *reinterpret_cast<volatile uint32_t*>(p.parity) & 1u;
+  __syncthreads();
+  grid_launch_dependents();
+  return par;
+}
+
+// Segment range of head hd for the call with parity par.
+__device__ __forceinline__ int2 head_segments(const DecodeParams& p, int hd, uint32_t par) {
+  const int4 h = p.hseg[hd];
+  return par ? make_int2(h.z, h.w) : make_int2(h.x, h.y);
+}
+
 // --------------------------------------------------------------------------
 // Reduce kernels (the reduce of src/kernel_triton.py:120-174, planned on the
 // device).  Row r = (head r / G, query head r % G) of a head whose pages fall
@@ -1147,9 +1196,9 @@ __global__ void __launch_bounds__(128) reduce_heads_kernel(const DecodeParams p)
   const int G = p.G, GD = G * D, nf = GD / 4;
   const int n_heads = p.B * p.Hkv;
   const int hd = blockIdx.x * 4 + (threadIdx.x >> 5);
-  grid_dependency_wait();  // partials written by the decode grid
+  const uint32_t par = reduce_prologue(p);
   if (hd >= n_heads) return;
-  const int2 hs = p.hseg[hd];
+  const int2 hs = head_segments(p, hd, par);
   if (hs.y <= 1) return;  // empty, or written whole by the decode kernel
   const int sf = p.slot_floats;
   const float* base = p.part + static_cast<int64_t>(hd + hs.x) * sf;
@@ -1225,10 +1274,10 @@ __global__ void __launch_bounds__(128) reduce_rows_kernel(const DecodeParams p) 
   const int G = p.G;
   const int rows = p.B * p.Hkv * G;
   const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
-  grid_dependency_wait();  // partials written by the decode grid
+  const uint32_t par = reduce_prologue(p);
   if (r >= rows) return;
   const int hd = r / G, g = r - hd * G;
-  const int2 hs = p.hseg[hd];
+  const int2 hs = head_segments(p, hd, par);
   if (hs.y <= 1) return;  // empty, or written whole by the decode kernel
   const float* bs1[1] = {p.part + static_cast<int64_t>(hd + hs.x) * p.slot_floats};
   const int g1[1] = {g}, a1[1] = {0}, b1[1] = {hs.y};
@@ -1249,9 +1298,9 @@ __global__ void __launch_bounds__(128) reduce_split_kernel(const DecodeParams p)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G;
   const int r = blockIdx.x;
-  grid_dependency_wait();  // partials written by the decode grid
+  const uint32_t par = reduce_prologue(p);
   const int hd = r / G, g = r - hd * G;
-  const int2 hs = p.hseg[hd];
+  const int2 hs = head_segments(p, hd, par);
   if (hs.y <= 1) return;  // uniform across the CTA
   constexpr int NC = (D + 127) / 128;
   const int a = static_cast<int>(static_cast<int64_t>(warp) * hs.y / 4);

@@ -158,7 +158,7 @@ struct Plan {
   int n_heads;
   int slot_floats;
   int steal_m_max;
-  size_t off_cum, off_wstart, off_claims, off_hseg, off_part, ws_bytes;
+  size_t off_cum, off_wstart, off_claims, off_hseg, off_empty, off_part, ws_bytes;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -340,8 +340,9 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   // Partial-state slot: acc [G][D], m [G], l [G].
   pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
   // Workspace: status, weff and the dynamic-tail header in the first 256
-  // bytes, then cum, wstart, claim words, per-head segment ranges and the
-  // partial slots
+  // bytes (status, weff, parity of the current call, dynamic-tail header),
+  // then cum, wstart, claim words, per-head segment ranges for two calls,
+  // the list of empty heads and the partial slots
   // (n_heads + W * (m_max + 1): one per (head, segment) pair).  The tail
   // chunk count per warp is capped so that the workspace stays within the
   // 16 MiB of the no-alloc scratch.
@@ -356,7 +357,9 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
     pl->off_claims = off;
     off = align256(off + size_t(W) * 8);
     pl->off_hseg = off;
-    off = align256(off + size_t(pl->n_heads) * 8);
+    off = align256(off + size_t(pl->n_heads) * 16);
+    pl->off_empty = off;
+    off = align256(off + size_t(pl->n_heads) * 4);
     pl->off_part = off;
     off = align256(off + (size_t(pl->n_heads) + size_t(W) * (m_max + 1)) * pl->slot_floats * 4);
     pl->ws_bytes = off;
@@ -422,10 +425,14 @@ int encode_cache_map_uncached(const pab200_decode_args* a, const void* base, CUt
   return PAB200_OK;
 }
 
+// The planner is launched with programmatic dependent launch: after the
+// previous call on this stream (whose reduce kernel lets it start once that
+// kernel has read its parity) it overlaps that reduce, and it waits for it
+// before completing.
 template <typename T>
-cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s) {
-  pab::plan_kernel<T><<<1, 1024, 0, s>>>(p);
-  return cudaGetLastError();
+cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s, bool pdl) {
+  LaunchCfg lc(dim3(1), dim3(1024), 0, s, pdl);
+  return cudaLaunchKernelEx(&lc.cfg, pab::plan_kernel<T>, p);
 }
 
 
@@ -530,7 +537,10 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   p.weff = reinterpret_cast<int32_t*>(ws + 4);
   p.steal = reinterpret_cast<int32_t*>(ws + 16);
   p.claims = reinterpret_cast<unsigned long long*>(ws + pl.off_claims);
-  p.hseg = reinterpret_cast<int2*>(ws + pl.off_hseg);
+  p.hseg = reinterpret_cast<int4*>(ws + pl.off_hseg);
+  p.parity = reinterpret_cast<uint32_t*>(ws + 8);
+  p.n_empty = reinterpret_cast<int32_t*>(ws + 12);
+  p.empty = reinterpret_cast<int32_t*>(ws + pl.off_empty);
   p.steal_m_max = pl.steal_m_max;
   p.steal_pps = pl.st / a->block_size;
   p.cum = reinterpret_cast<int32_t*>(ws + pl.off_cum);
@@ -551,14 +561,14 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
     vmap = CUtensorMap{};
   }
 
-  cudaError_t e = a->dtype == PAB200_DTYPE_BF16 ? launch_plan<__nv_bfloat16>(p, s)
-                                                 : launch_plan<__half>(p, s);
+  const bool pdl = env_int("PAB200_PDL", 1) != 0;
+  cudaError_t e = a->dtype == PAB200_DTYPE_BF16 ? launch_plan<__nv_bfloat16>(p, s, pdl)
+                                                 : launch_plan<__half>(p, s, pdl);
   if (e != cudaSuccess) return cuda_fail(e, "plan kernel launch");
   if (a->event_before) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_before), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  const bool pdl = env_int("PAB200_PDL", 1) != 0;
   e = pl.ops.launch(dim3(pl.grid), dim3(pl.wpc * 32), pl.smem, s, pdl && !a->event_before, kmap,
                     vmap, p);
   if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");

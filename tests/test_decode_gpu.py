@@ -138,3 +138,37 @@ def test_cuda_core_path_vs_oracle(cuda_device, monkeypatch, steal_m, B, Hkv, G, 
     dev = cuda_device
     out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
     assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"CUDA-core G{G} D{D} bs{bs}")
+
+
+def test_cuda_graph_replay_follows_inputs(cuda_device):
+    """The whole call (planner, decode, reduce) captured once in a CUDA graph
+    and replayed after the inputs changed in place (new queries, new lengths)
+    gives the eager result: the plan is made on the device from the current
+    lengths at every replay, and no host work sits inside the call."""
+    dev = cuda_device
+    lens0 = [[900, 33], [4000, 1], [17, 2500]]
+    q, k, v, sl, bt, scale = random_case(3, 2, 4, 128, 16, lens0, torch.bfloat16, seed=91)
+    q, k, v, sl, bt = (t.to(dev) for t in (q, k, v, sl, bt))
+    fn = _b200()
+    fn(q, k, v, sl, bt, scale)  # allocates and caches the workspace outside capture
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn(q, k, v, sl, bt, scale)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            out = fn(q, k, v, sl, bt, scale)
+    torch.cuda.synchronize()
+    g = torch.Generator(device=dev).manual_seed(5)
+    # new lengths stay within each head's allocated pages (the block table is unchanged)
+    for new_lens in ([[900, 33], [4000, 1], [17, 2500]], [[500, 0], [3999, 1], [16, 2048]]):
+        q.copy_(torch.randn(q.shape, generator=g, device=dev, dtype=torch.float32).to(q.dtype))
+        sl.copy_(torch.tensor(new_lens, dtype=sl.dtype, device=dev))
+        graph.replay()
+        torch.cuda.synchronize()
+        eager = fn(q, k, v, sl, bt, scale)
+        assert torch.equal(out, eager), new_lens
+        assert_close(out.cpu(), run_oracle(q.cpu(), k.cpu(), v.cpu(), sl.cpu(), bt.cpu(), scale),
+                     what=f"graph replay {new_lens}")

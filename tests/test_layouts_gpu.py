@@ -155,3 +155,39 @@ def test_states_merge_both_arithmetic_paths(cuda_device, monkeypatch, core):
         paged_attention_states(q.to(dev), pk.to(dev), pv.to(dev), btl.to(dev), ll.to(dev), scale,
                                bs, state=states[r])
     assert_close(merge_packed_states(states, B, Hkv * G, D), ref, what=f"core={core}")
+
+
+@pytest.mark.parametrize("state_mode", [False, True])
+def test_back_to_back_calls_reuse_outputs(cuda_device, state_mode):
+    """Calls queued back to back on one stream into the same output: the
+    next call's planner may overlap the previous call's reduce kernel, so a
+    head that was split across warps in one call and is empty in the next
+    must still end up zero (and an empty state: o = 0, lse = -inf), and
+    every other head must hold the new call's result."""
+    B, Hkv, G, D, bs = 4, 2, 4, 128, 16
+    long_lens = [6000, 5000, 7000, 4000]
+    q, pk, pv, bt, lens, scale = _pool_case(B, Hkv, G, D, bs, long_lens, torch.bfloat16, seed=21)
+    dev = cuda_device
+    qd, kd, vd, btd = q.to(dev), pk.to(dev), pv.to(dev), bt.to(dev)
+    rounds = [long_lens, [0, 5000, 0, 4000], long_lens, [6000, 0, 7000, 0]]
+    lens_d = [torch.tensor(x, dtype=torch.int32, device=dev) for x in rounds]
+    if state_mode:
+        state = torch.empty(state_numel(B, Hkv * G, D), dtype=torch.float32, device=dev)
+        for ld in lens_d:  # no synchronisation between the calls
+            paged_attention_states(qd, kd, vd, btd, ld, scale, bs, state=state)
+        o = state[:B * Hkv * G * D].view(B, Hkv * G, D).cpu()
+        lse = state[B * Hkv * G * D:B * Hkv * G * (D + 1)].view(B, Hkv * G).cpu()
+        assert torch.count_nonzero(o[1]) == 0 and torch.count_nonzero(o[3]) == 0
+        assert bool(torch.isneginf(lse[1]).all()) and bool(torch.isneginf(lse[3]).all())
+        got = o[[0, 2]]
+    else:
+        out = torch.empty_like(qd)
+        for ld in lens_d:  # no synchronisation between the calls
+            paged_attention(out, qd, kd, vd, btd, ld, scale, bs)
+        out = out.cpu()
+        assert torch.count_nonzero(out[1]) == 0 and torch.count_nonzero(out[3]) == 0
+        got = out[[0, 2]]
+    last = torch.tensor(rounds[-1], dtype=torch.int32)
+    q4, kp, vp, sl, bt3 = _reference_view(q, pk, pv, bt, last)
+    ref = run_oracle(q4, kp, vp, sl, bt3, scale)[:, 0]
+    assert_close(got.float(), ref[[0, 2]], what="back-to-back calls")
