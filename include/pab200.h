@@ -75,6 +75,7 @@ typedef enum pab200_layout {
 #define PAB200_STATUS_SEQLEN_CLAMP 0x2u  /* seqlen > max_blocks*block_size    */
 #define PAB200_STATUS_NEG_SEQLEN 0x4u    /* seqlen < 0 (treated as 0)         */
 #define PAB200_STATUS_WAIT_TIMEOUT 0x8u  /* a pipeline wait hit its time limit */
+#define PAB200_STATUS_APPEND_FULL 0x10u  /* kv append: no page slot left (L >= max_blocks*block_size) */
 
 /* Arguments of one batched paged decode call.
  *
@@ -262,6 +263,40 @@ int pab200_exchange_merge(const float* state, void* const* bufs, int32_t rank,
                           int32_t world, int64_t rows, int32_t head_size,
                           void* out, int64_t out_stride_row, int32_t out_dtype,
                           int64_t wait_limit_ns, uint32_t* status, void* stream);
+
+/* Arguments of pab200_kv_append(): the step before a decode, writing each
+ * (sequence, kv head)'s new token into its page.  Cache layout, block-table
+ * addressing and seqlens strides mean what they mean in pab200_decode_args. */
+typedef struct pab200_kv_append_args {
+  void* k_cache;             /* see pab200_layout                              */
+  void* v_cache;
+  const void* k_new;         /* [num_seqs, num_kv_heads, head_size], dtype     */
+  const void* v_new;
+  int32_t* seqlens;          /* current lengths L; L + 1 afterwards if increment */
+  const int32_t* block_table;
+  uint32_t* status;          /* device word: PAB200_STATUS_* bits ORed in; may be null */
+
+  int32_t dtype, layout;
+  int32_t num_seqs, num_kv_heads, head_size, block_size, max_blocks;
+  int64_t num_pages;
+  int64_t new_stride_b, new_stride_h;          /* of k_new / v_new; head_size stride 1 */
+  int64_t seqlens_stride_b, seqlens_stride_h;  /* h stride 0 => per-seq length        */
+  int64_t bt_stride_b, bt_stride_h, bt_stride_i;
+  int32_t bt_page_mul, bt_page_add;
+  int32_t increment;         /* 1: seqlens[s, h] += 1 after the write             */
+} pab200_kv_append_args;
+
+/* KV append.  No counterpart in the reference (its decode only reads the
+ * cache; its benchmark fills the cache once, scripts/benchmark.py:101-108):
+ * for every (sequence s, kv head h) with current length L = seqlens(s,h),
+ * writes k_new[s,h,:] / v_new[s,h,:] into row L % block_size of page
+ * page(s,h,L / block_size) (the addressing of pab200_decode_args) and, with
+ * increment, stores L + 1.  A slot past max_blocks sets
+ * PAB200_STATUS_APPEND_FULL, a page id outside [0, num_pages) sets
+ * PAB200_STATUS_BAD_PAGE_ID, and that (s, h) is left untouched (length
+ * included).  With a per-sequence length (seqlens_stride_h == 0) the length
+ * is incremented once per sequence.  One launch, asynchronous on `stream`. */
+int pab200_kv_append(const pab200_kv_append_args* args, void* stream);
 
 /* Copy the device status word of `workspace` (the PAB200_STATUS_* bits raised
  * by the most recent pab200_decode call on it) to *status_out.  Synchronises

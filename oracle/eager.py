@@ -13,6 +13,10 @@ It restates, in numpy float32, the reference's eager PyTorch implementation
 * ``split_state`` / ``merge_states`` restate the split-KV partial state of
   src/kernel_triton.py:8-117 and its log-sum-exp merge,
   src/kernel_triton.py:120-174, used to check the cross-device path.
+* ``kv_append`` has no counterpart in the reference (which only reads the
+  cache): it states the write that precedes a decode step — the new token's
+  K and V go to row L % block_size of page block_table[L // block_size],
+  L being the current length — in the page layout of src/common.py:6-7.
 
 Parity is pinned: tests/golden/ holds vectors produced by importing the
 reference's own ``flash_attn_with_kvcache_wrapper_eager`` (fp32, CPU), and
@@ -164,3 +168,35 @@ def kv_bytes(cache_seqlens, head_size: int, elt_bytes: int) -> int:
 
 def default_scale(head_size: int) -> float:
     return 1.0 / math.sqrt(head_size)
+
+
+def kv_append(k_cache, v_cache, k_new, v_new, cache_seqlens, block_table, increment=True):
+    """Write each (sequence, kv head)'s new token into its page (in place).
+
+    k_cache/v_cache: [num_pages, block_size, D] (src/common.py:6-7); k_new,
+    v_new: [B, Hkv, D]; cache_seqlens: [B, Hkv] (current lengths L);
+    block_table: [B, Hkv, max_blocks].  Row L % block_size of page
+    block_table[s, h, L // block_size] receives the token; with ``increment``
+    the length becomes L + 1.  A (sequence, kv head) whose L is negative,
+    whose page slot lies past max_blocks or whose page id is outside the cache
+    is left untouched.  No counterpart in the reference.
+    """
+    k_cache, v_cache = np.asarray(k_cache), np.asarray(v_cache)
+    k_new, v_new = np.asarray(k_new), np.asarray(v_new)
+    lens = np.asarray(cache_seqlens).copy()
+    bt = np.asarray(block_table)
+    num_pages, bs, _ = k_cache.shape
+    B, Hkv = lens.shape
+    for s in range(B):
+        for h in range(Hkv):
+            L = int(lens[s, h])
+            if L < 0 or L // bs >= bt.shape[2]:
+                continue
+            page = int(bt[s, h, L // bs])
+            if not 0 <= page < num_pages:
+                continue
+            k_cache[page, L % bs] = k_new[s, h]
+            v_cache[page, L % bs] = v_new[s, h]
+            if increment:
+                lens[s, h] = L + 1
+    return lens

@@ -8,6 +8,8 @@ from .common import _validate_decode_inputs
 from .kernel_b200 import (
     default_scale,
     flash_attn_with_kvcache_wrapper_b200,
+    kv_append,
+    kv_append_status,
     merge_packed_states,
     merge_states,
     paged_attention,
@@ -20,6 +22,8 @@ __all__ = [
     "_validate_decode_inputs",
     "default_scale",
     "flash_attn_with_kvcache_wrapper_b200",
+    "kv_append",
+    "kv_append_status",
     "merge_packed_states",
     "merge_states",
     "paged_attention",

@@ -39,6 +39,7 @@ STATUS_BAD_PAGE_ID = 0x1
 STATUS_SEQLEN_CLAMP = 0x2
 STATUS_NEG_SEQLEN = 0x4
 STATUS_WAIT_TIMEOUT = 0x8
+STATUS_APPEND_FULL = 0x10
 
 EXPORTED_SYMBOLS = (
     "pab200_decode_workspace_size",
@@ -47,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "pab200_decode_noalloc",
     "pab200_paged_attention",
     "pab200_merge_states",
+    "pab200_kv_append",
     "pab200_exchange_buffer_bytes",
     "pab200_exchange_buffer_create",
     "pab200_exchange_buffer_open",
@@ -59,6 +61,38 @@ EXPORTED_SYMBOLS = (
     "pab200_last_error",
     "pab200_abi_version",
 )
+
+
+class KvAppendArgs(ctypes.Structure):
+    """Mirror of ``pab200_kv_append_args`` (field order and types must match)."""
+
+    _fields_ = [
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("k_new", ctypes.c_void_p),
+        ("v_new", ctypes.c_void_p),
+        ("seqlens", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("layout", ctypes.c_int32),
+        ("num_seqs", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_size", ctypes.c_int32),
+        ("block_size", ctypes.c_int32),
+        ("max_blocks", ctypes.c_int32),
+        ("num_pages", ctypes.c_int64),
+        ("new_stride_b", ctypes.c_int64),
+        ("new_stride_h", ctypes.c_int64),
+        ("seqlens_stride_b", ctypes.c_int64),
+        ("seqlens_stride_h", ctypes.c_int64),
+        ("bt_stride_b", ctypes.c_int64),
+        ("bt_stride_h", ctypes.c_int64),
+        ("bt_stride_i", ctypes.c_int64),
+        ("bt_page_mul", ctypes.c_int32),
+        ("bt_page_add", ctypes.c_int32),
+        ("increment", ctypes.c_int32),
+    ]
 
 
 class DecodeArgs(ctypes.Structure):
@@ -133,6 +167,8 @@ def load() -> ctypes.CDLL:
         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
         ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.pab200_paged_attention.restype = ctypes.c_int
+    lib.pab200_kv_append.argtypes = [ctypes.POINTER(KvAppendArgs), ctypes.c_void_p]
+    lib.pab200_kv_append.restype = ctypes.c_int
     lib.pab200_merge_states.argtypes = [
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
         ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,

@@ -1394,6 +1394,72 @@ __global__ void __launch_bounds__(256) merge_states_kernel(
 }
 
 // --------------------------------------------------------------------------
+// KV append (the step before a decode; no counterpart in the reference).
+// One warp per sequence: for every kv head it reads the current length L,
+// copies the new K and V rows (head_size 2-byte elements as 32-bit words,
+// lanes over the words) into row L % bs of page block_table[L / bs], and only
+// then stores the new lengths, so a length shared by all heads of a sequence
+// (h stride 0) is read by every head before it changes.
+struct AppendParams {
+  uint32_t* k_cache;
+  uint32_t* v_cache;
+  const uint32_t* k_new;
+  const uint32_t* v_new;
+  int32_t* lens;
+  const int32_t* bt;
+  uint32_t* status;
+  int32_t B, Hkv, D, bs, maxb, head_in_page;  // head_in_page: NHD cache (Hkv rows per token)
+  int64_t num_pages;
+  int64_t n_sb, n_sh, l_sb, l_sh, bt_sb, bt_sh, bt_si;
+  int32_t bt_mul, bt_add, increment;
+};
+
+constexpr uint32_t kStatusAppendFull = 0x10u;
+
+__global__ void __launch_bounds__(128) kv_append_kernel(const AppendParams p) {
+  const int lane = threadIdx.x & 31;
+  const int s = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (s >= p.B) return;
+  const int words = p.D / 2;
+  const int hc_rows = p.head_in_page ? p.Hkv : 1;
+  uint32_t flags = 0;
+  bool all_ok = true;
+  for (int h = 0; h < p.Hkv; ++h) {
+    const int L = p.lens[s * p.l_sb + h * p.l_sh];
+    bool ok = L >= 0;
+    if (ok && L / p.bs >= p.maxb) {
+      flags |= kStatusAppendFull;
+      ok = false;
+    }
+    int64_t pid = 0;
+    if (ok) {
+      pid = static_cast<int64_t>(p.bt[s * p.bt_sb + h * p.bt_sh + static_cast<int64_t>(L / p.bs) * p.bt_si]) *
+                p.bt_mul + static_cast<int64_t>(h) * p.bt_add;
+      if (pid < 0 || pid >= p.num_pages) {
+        flags |= kStatusBadPage;
+        ok = false;
+      }
+    }
+    all_ok &= ok;
+    if (!ok) continue;
+    const int64_t row = (pid * p.bs + L % p.bs) * hc_rows + (p.head_in_page ? h : 0);
+    const uint32_t* kn = p.k_new + (s * p.n_sb + h * p.n_sh) / 2;
+    const uint32_t* vn = p.v_new + (s * p.n_sb + h * p.n_sh) / 2;
+    uint32_t* kd = p.k_cache + row * words;
+    uint32_t* vd = p.v_cache + row * words;
+    for (int w = lane; w < words; w += 32) {
+      kd[w] = kn[w];
+      vd[w] = vn[w];
+    }
+    if (p.increment && p.l_sh != 0 && lane == 0) p.lens[s * p.l_sb + h * p.l_sh] = L + 1;
+  }
+  // A length shared by the sequence's heads moves once, after every head
+  // has read it, and only if every head's token was written.
+  if (p.increment && p.l_sh == 0 && all_ok && lane == 0) p.lens[s * p.l_sb] += 1;
+  if (flags && lane == 0 && p.status) atomicOr(p.status, flags);
+}
+
+// --------------------------------------------------------------------------
 // Fused exchange + merge of partial states over peer memory (ranks of one
 // node, buffers mapped with CUDA IPC).  Replaces all-gather + merge_states for
 // a context split across GPUs.

@@ -819,6 +819,52 @@ PAB200_EXPORT int pab200_exchange_merge(const float* state, void* const* bufs, i
   return PAB200_OK;
 }
 
+PAB200_EXPORT int pab200_kv_append(const pab200_kv_append_args* a, void* stream) {
+  if (!a) return fail(PAB200_ERR_INVALID_ARGUMENT, "args is null");
+  if (a->dtype != PAB200_DTYPE_BF16 && a->dtype != PAB200_DTYPE_F16)
+    return fail(PAB200_ERR_UNSUPPORTED, "dtype %d: caches must be bf16 or f16", a->dtype);
+  if (a->layout != PAB200_LAYOUT_PAGES && a->layout != PAB200_LAYOUT_NHD)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "unknown cache layout %d", a->layout);
+  if (a->num_seqs < 0 || a->num_kv_heads < 1 || a->block_size < 1 || a->max_blocks < 1 ||
+      a->head_size < 2 || (a->head_size & 1) || a->num_pages < 0)
+    return fail(PAB200_ERR_INVALID_ARGUMENT,
+                "need num_seqs >= 0, num_kv_heads, block_size, max_blocks >= 1, even head_size");
+  if (a->num_seqs == 0) return PAB200_OK;
+  if (!a->k_cache || !a->v_cache || !a->k_new || !a->v_new || !a->seqlens || !a->block_table)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned(a->k_cache, 4) || !aligned(a->v_cache, 4) || !aligned(a->k_new, 4) ||
+      !aligned(a->v_new, 4) || (a->new_stride_b & 1) || (a->new_stride_h & 1))
+    return fail(PAB200_ERR_ALIGNMENT, "caches and new rows 4-byte aligned, even strides");
+  pab::AppendParams p{};
+  p.k_cache = static_cast<uint32_t*>(a->k_cache);
+  p.v_cache = static_cast<uint32_t*>(a->v_cache);
+  p.k_new = static_cast<const uint32_t*>(a->k_new);
+  p.v_new = static_cast<const uint32_t*>(a->v_new);
+  p.lens = a->seqlens;
+  p.bt = a->block_table;
+  p.status = a->status;
+  p.B = a->num_seqs;
+  p.Hkv = a->num_kv_heads;
+  p.D = a->head_size;
+  p.bs = a->block_size;
+  p.maxb = a->max_blocks;
+  p.head_in_page = a->layout == PAB200_LAYOUT_NHD ? 1 : 0;
+  p.num_pages = a->num_pages;
+  p.n_sb = a->new_stride_b;
+  p.n_sh = a->new_stride_h;
+  p.l_sb = a->seqlens_stride_b;
+  p.l_sh = a->seqlens_stride_h;
+  p.bt_sb = a->bt_stride_b;
+  p.bt_sh = a->bt_stride_h;
+  p.bt_si = a->bt_stride_i;
+  p.bt_mul = a->bt_page_mul;
+  p.bt_add = a->bt_page_add;
+  p.increment = a->increment ? 1 : 0;
+  pab::kv_append_kernel<<<(a->num_seqs + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PAB200_OK : cuda_fail(e, "kv append launch");
+}
+
 PAB200_EXPORT int pab200_read_status(const void* workspace, uint32_t* status_out, void* stream) {
   if (!workspace || !status_out) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -436,3 +436,110 @@ def read_status(device=None) -> int:
 
 def default_scale(head_size: int) -> float:
     return 1.0 / math.sqrt(head_size)
+
+
+_append_status: dict[int, torch.Tensor] = {}
+
+
+def _append_status_word(device) -> torch.Tensor:
+    w = _append_status.get(device.index)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=device)
+        _append_status[device.index] = w
+    return w
+
+
+def kv_append(key_cache, value_cache, k_new, v_new, cache_seqlens, block_table, increment=True,
+              kv_layout="HND"):
+    """Write each (sequence, kv head)'s new token into its page, in place.
+
+    The step before a decode call; the reference has no counterpart (its
+    cache is filled once by its benchmark).  Caches and tables as for
+    ``paged_attention``: a 3-D reference page cache (num_pages, block_size,
+    head_size) with block_table (num_seqs, num_kv_heads, max_blocks), or a
+    4-D pool ("HND" (num_blocks, num_kv_heads, block_size, head_size) or
+    "NHD" (num_blocks, block_size, num_kv_heads, head_size)) with
+    block_table (num_seqs, max_blocks).  k_new, v_new: (num_seqs,
+    num_kv_heads, head_size).  cache_seqlens: int32 (num_seqs,) or
+    (num_seqs, num_kv_heads), the current lengths L; the token goes to row
+    L % block_size of page block_table[..., L // block_size] and, with
+    ``increment``, L becomes L + 1 (in place).  A full table or an invalid
+    page id leaves that entry untouched and sets a bit read by
+    ``kv_append_status``.
+    """
+    if tuple(key_cache.shape) != tuple(value_cache.shape):
+        raise ValueError("key_cache and value_cache shapes differ")
+    if key_cache.dtype not in _DTYPES or value_cache.dtype != key_cache.dtype:
+        raise TypeError("caches must share one dtype, bfloat16 or float16")
+    if k_new.dtype != key_cache.dtype or v_new.dtype != key_cache.dtype:
+        raise TypeError("k_new and v_new must have the caches' dtype")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("key_cache and value_cache must be contiguous")
+    if k_new.dim() != 3 or tuple(k_new.shape) != tuple(v_new.shape):
+        raise ValueError("k_new and v_new must be (num_seqs, num_kv_heads, head_size)")
+    if k_new.stride(2) != 1 or v_new.stride(2) != 1 or k_new.stride() != v_new.stride():
+        raise ValueError("k_new and v_new must share strides, contiguous in head_size")
+    if cache_seqlens.dtype != torch.int32:
+        raise TypeError("cache_seqlens must be int32 (it is updated in place)")
+    bt = _as_int32(block_table, "block_table")
+    B, Hkv, D = k_new.shape
+    a = _lib.KvAppendArgs()
+    if key_cache.dim() == 3:
+        if bt.dim() != 3 or tuple(bt.shape[:2]) != (B, Hkv):
+            raise ValueError("a 3-D cache needs block_table (num_seqs, num_kv_heads, max_blocks)")
+        num_pages, bs, Dc = key_cache.shape
+        layout, mul, add = _lib.LAYOUT_PAGES, 1, 0
+        sb, sh, si, maxb = bt.stride(0), bt.stride(1), bt.stride(2), bt.shape[2]
+    elif key_cache.dim() == 4 and kv_layout in ("HND", "NHD"):
+        if bt.dim() != 2 or bt.shape[0] != B:
+            raise ValueError("a 4-D pool needs block_table (num_seqs, max_blocks)")
+        if kv_layout == "HND":
+            nb, Hc, bs, Dc = key_cache.shape
+            num_pages, layout, mul, add = nb * Hc, _lib.LAYOUT_PAGES, Hc, 1
+        else:
+            nb, bs, Hc, Dc = key_cache.shape
+            num_pages, layout, mul, add = nb, _lib.LAYOUT_NHD, 1, 0
+        if Hc != Hkv:
+            raise ValueError(f"cache has {Hc} kv heads, k_new {Hkv}")
+        sb, sh, si, maxb = bt.stride(0), 0, bt.stride(1), bt.shape[1]
+    else:
+        raise ValueError(f"unsupported cache rank {key_cache.dim()} / kv_layout {kv_layout!r}")
+    if Dc != D:
+        raise ValueError(f"cache head_size {Dc} != k_new head_size {D}")
+    lens = cache_seqlens
+    if lens.dim() == 1 and lens.shape[0] == B:
+        lsb, lsh = lens.stride(0), 0
+    elif lens.dim() == 2 and tuple(lens.shape) == (B, Hkv):
+        lsb, lsh = lens.stride(0), lens.stride(1)
+    else:
+        raise ValueError("cache_seqlens must be (num_seqs,) or (num_seqs, num_kv_heads)")
+    device = _check_device(key_cache, value_cache, k_new, v_new, lens, bt)
+    status = _append_status_word(device)
+    a.k_cache, a.v_cache = key_cache.data_ptr(), value_cache.data_ptr()
+    a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
+    a.seqlens, a.block_table, a.status = lens.data_ptr(), bt.data_ptr(), status.data_ptr()
+    a.dtype, a.layout = _DTYPES[key_cache.dtype], layout
+    a.num_seqs, a.num_kv_heads, a.head_size, a.block_size = B, Hkv, D, bs
+    a.max_blocks, a.num_pages = maxb, num_pages
+    a.new_stride_b, a.new_stride_h = k_new.stride(0), k_new.stride(1)
+    a.seqlens_stride_b, a.seqlens_stride_h = lsb, lsh
+    a.bt_stride_b, a.bt_stride_h, a.bt_stride_i = sb, sh, si
+    a.bt_page_mul, a.bt_page_add = mul, add
+    a.increment = 1 if increment else 0
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        rc = lib.pab200_kv_append(ctypes.byref(a), ctypes.c_void_p(_current_stream_handle(device)))
+    _lib.check(lib, rc, "pab200_kv_append")
+    del bt
+
+
+def kv_append_status(device=None, reset=True) -> int:
+    """PAB200_STATUS_* bits raised by kv_append calls on ``device`` since the
+    last reset (synchronises the device)."""
+    device = torch.device("cuda", torch.cuda.current_device() if device is None else
+                          torch.device(device).index)
+    w = _append_status_word(device)
+    bits = int(w.item())
+    if reset:
+        w.zero_()
+    return bits
