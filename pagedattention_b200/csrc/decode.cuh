@@ -1544,8 +1544,11 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const ExchangeParam
   const int64_t r1 = r0 + p.rows_per_block < rows ? r0 + p.rows_per_block : rows;
   uint32_t* epochs = reinterpret_cast<uint32_t*>(p.bufs[rank] + 2 * world * S);
   // `state` (and, after a previous exchange, `epochs`) were written by the
-  // preceding grid on this stream: read them only after it has completed
+  // preceding grid on this stream: read them only after it has completed.
+  // The next call's planner may then start: it writes nothing this kernel
+  // reads, and it waits for this kernel before it completes.
   grid_dependency_wait();
+  grid_launch_dependents();
   const uint32_t e = reinterpret_cast<volatile uint32_t*>(epochs)[b] + 1u;
   const int par = e & 1;
   // 1. store rows [r0, r1) of o and lse into every peer's slot [par][rank]
