@@ -1395,11 +1395,13 @@ __global__ void __launch_bounds__(256) merge_states_kernel(
 
 // --------------------------------------------------------------------------
 // KV append (the step before a decode; no counterpart in the reference).
-// One warp per sequence: for every kv head it reads the current length L,
-// copies the new K and V rows (head_size 2-byte elements as 32-bit words,
-// lanes over the words) into row L % bs of page block_table[L / bs], and only
-// then stores the new lengths, so a length shared by all heads of a sequence
-// (h stride 0) is read by every head before it changes.
+// One warp per sequence.  Lane h (per group of 32 kv heads) reads head h's
+// current length L and its page id together, so every head's length is read
+// before any changes; the new K and V rows (head_size 2-byte elements copied
+// as 32-bit words, lanes over the words) are then copied four heads at a
+// time with their loads in flight together, into row L % bs of page
+// block_table[L / bs]; last, the lengths move.  A length shared by all heads
+// of a sequence (h stride 0) moves once, if every head's token was written.
 struct AppendParams {
   uint32_t* k_cache;
   uint32_t* v_cache;
@@ -1424,38 +1426,66 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const AppendParams p) {
   const int hc_rows = p.head_in_page ? p.Hkv : 1;
   uint32_t flags = 0;
   bool all_ok = true;
-  for (int h = 0; h < p.Hkv; ++h) {
-    const int L = p.lens[s * p.l_sb + h * p.l_sh];
-    bool ok = L >= 0;
-    if (ok && L / p.bs >= p.maxb) {
-      flags |= kStatusAppendFull;
-      ok = false;
-    }
-    int64_t pid = 0;
-    if (ok) {
-      pid = static_cast<int64_t>(p.bt[s * p.bt_sb + h * p.bt_sh + static_cast<int64_t>(L / p.bs) * p.bt_si]) *
-                p.bt_mul + static_cast<int64_t>(h) * p.bt_add;
-      if (pid < 0 || pid >= p.num_pages) {
-        flags |= kStatusBadPage;
+  for (int h0 = 0; h0 < p.Hkv; h0 += 32) {
+    // lane h: head h0 + h's length, page and destination row
+    const int h = h0 + lane;
+    int L = -1;
+    bool ok = false;
+    int64_t row = 0;
+    if (h < p.Hkv) {
+      L = p.lens[s * p.l_sb + h * p.l_sh];
+      ok = L >= 0;
+      if (ok && L / p.bs >= p.maxb) {
+        flags |= kStatusAppendFull;
         ok = false;
       }
+      if (ok) {
+        const int64_t pid =
+            static_cast<int64_t>(p.bt[s * p.bt_sb + h * p.bt_sh + static_cast<int64_t>(L / p.bs) * p.bt_si]) *
+                p.bt_mul + static_cast<int64_t>(h) * p.bt_add;
+        if (pid < 0 || pid >= p.num_pages) {
+          flags |= kStatusBadPage;
+          ok = false;
+        }
+        row = (pid * p.bs + L % p.bs) * hc_rows + (p.head_in_page ? h : 0);
+      }
     }
-    all_ok &= ok;
-    if (!ok) continue;
-    const int64_t row = (pid * p.bs + L % p.bs) * hc_rows + (p.head_in_page ? h : 0);
-    const uint32_t* kn = p.k_new + (s * p.n_sb + h * p.n_sh) / 2;
-    const uint32_t* vn = p.v_new + (s * p.n_sb + h * p.n_sh) / 2;
-    uint32_t* kd = p.k_cache + row * words;
-    uint32_t* vd = p.v_cache + row * words;
-    for (int w = lane; w < words; w += 32) {
-      kd[w] = kn[w];
-      vd[w] = vn[w];
+    all_ok &= __all_sync(0xffffffffu, ok || h >= p.Hkv);
+    const int nh = min(32, p.Hkv - h0);
+    for (int c0 = 0; c0 < nh; c0 += 4) {
+      uint32_t kw[4][4], vw[4][4];  // 4 heads x up to 4 words per lane (head_size <= 256)
+      bool hok[4];
+      int64_t hrow[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u < nh ? c0 + u : nh - 1;
+        hok[u] = __shfl_sync(0xffffffffu, ok, c) && c0 + u < nh;
+        hrow[u] = __shfl_sync(0xffffffffu, row, c);
+        const int64_t src = (s * p.n_sb + static_cast<int64_t>(h0 + c) * p.n_sh) / 2;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int w = lane + 32 * q;
+          kw[u][q] = hok[u] && w < words ? p.k_new[src + w] : 0u;
+          vw[u][q] = hok[u] && w < words ? p.v_new[src + w] : 0u;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (!hok[u]) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int w = lane + 32 * q;
+          if (w < words) {
+            p.k_cache[hrow[u] * words + w] = kw[u][q];
+            p.v_cache[hrow[u] * words + w] = vw[u][q];
+          }
+        }
+      }
     }
-    if (p.increment && p.l_sh != 0 && lane == 0) p.lens[s * p.l_sb + h * p.l_sh] = L + 1;
+    if (p.increment && p.l_sh != 0 && ok) p.lens[s * p.l_sb + h * p.l_sh] = L + 1;
   }
-  // A length shared by the sequence's heads moves once, after every head
-  // has read it, and only if every head's token was written.
   if (p.increment && p.l_sh == 0 && all_ok && lane == 0) p.lens[s * p.l_sb] += 1;
+  flags = __reduce_or_sync(0xffffffffu, flags);
   if (flags && lane == 0 && p.status) atomicOr(p.status, flags);
 }
 

@@ -826,9 +826,9 @@ PAB200_EXPORT int pab200_kv_append(const pab200_kv_append_args* a, void* stream)
   if (a->layout != PAB200_LAYOUT_PAGES && a->layout != PAB200_LAYOUT_NHD)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "unknown cache layout %d", a->layout);
   if (a->num_seqs < 0 || a->num_kv_heads < 1 || a->block_size < 1 || a->max_blocks < 1 ||
-      a->head_size < 2 || (a->head_size & 1) || a->num_pages < 0)
+      a->head_size < 2 || (a->head_size & 1) || a->head_size > 256 || a->num_pages < 0)
     return fail(PAB200_ERR_INVALID_ARGUMENT,
-                "need num_seqs >= 0, num_kv_heads, block_size, max_blocks >= 1, even head_size");
+                "need num_seqs >= 0, num_kv_heads, block_size, max_blocks >= 1, even head_size <= 256");
   if (a->num_seqs == 0) return PAB200_OK;
   if (!a->k_cache || !a->v_cache || !a->k_new || !a->v_new || !a->seqlens || !a->block_table)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
