@@ -381,17 +381,17 @@ def run_b200(args):
 
     # The same calls captured once in a CUDA graph and replayed: the device
     # time per call without any host work (one captured call per cache copy,
-    # so the L2 rotation is kept).  Not for the context split, whose exchange
-    # spans processes.
+    # so the L2 rotation is kept).  One GPU only: no process group is active
+    # while the stream is captured.
     graph_line = None
-    if mode != "split":
+    if world == 1:
         gstream = torch.cuda.Stream(dev)
         gstream.wait_stream(torch.cuda.current_stream(dev))
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.stream(gstream):
             step()
             gstream.synchronize()
-            with torch.cuda.graph(graph, stream=gstream):
+            with torch.cuda.graph(graph, stream=gstream, capture_error_mode="thread_local"):
                 for _ in range(copies):
                     step()
         torch.cuda.current_stream(dev).wait_stream(gstream)
