@@ -172,3 +172,29 @@ def test_cuda_graph_replay_follows_inputs(cuda_device):
         assert torch.equal(out, eager), new_lens
         assert_close(out.cpu(), run_oracle(q.cpu(), k.cpu(), v.cpu(), sl.cpu(), bt.cpu(), scale),
                      what=f"graph replay {new_lens}")
+
+
+def test_many_short_sequences(cuda_device):
+    """2048 sequences x 8 kv heads of 1-64 tokens: 16k heads, many of them
+    in each warp's range (the planner's per-thread head runs and the
+    head-window walk), plus empty heads scattered through the batch."""
+    g = torch.Generator().manual_seed(17)
+    lens = torch.randint(0, 65, (2048, 8), generator=g, dtype=torch.int32)
+    q, k, v, sl, bt, scale = random_case(2048, 8, 4, 128, 16, lens, torch.bfloat16, seed=17,
+                                         poison=False)
+    dev = cuda_device
+    out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
+    assert_close(out, run_oracle(q, k, v, sl, bt, scale), what="2048 short sequences")
+
+
+def test_one_long_sequence_over_every_warp(cuda_device):
+    """One sequence, one kv head, 200k tokens: a single head cut into a
+    static prefix and tail chunks on every warp, merged from ~1000 partial
+    states (the CTA-per-row reduce)."""
+    q, k, v, sl, bt, scale = random_case(1, 1, 8, 128, 16, [[200_000]], torch.bfloat16, seed=23,
+                                         poison=False)
+    dev = cuda_device
+    out = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
+    assert_close(out, run_oracle(q, k, v, sl, bt, scale), what="one 200k-token head")
+    again = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
+    assert torch.equal(out, again)
