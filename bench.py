@@ -39,6 +39,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "KV-cache read GB/s (% of B200 HBM peak) and µs per paged-decode call"
 UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
+DATASHEET_HBM_GBS = 8000.0  # B200 HBM3e nominal (DGX figure), for context
 
 
 def parse_args():
@@ -478,6 +479,11 @@ def run_b200(args):
         exchange.close()
         if exchange_status:
             raise SystemExit(f"rank {rank}: peer exchange status {exchange_status:#x}")
+    # bytes moved besides the K/V pages (this rank's call): q read, output
+    # written, block-table entries and lengths read
+    extra_bytes = {"q": q.numel() * q.element_size(), "out": q.numel() * q.element_size(),
+                   "block_table": int(((sl.to(torch.int64) + w.block_size - 1) // w.block_size).sum()) * 4,
+                   "seqlens": sl.numel() * sl.element_size()}
     peak, peak_src = hbm_peak()
     traffic, traffic_src = ncu_traffic(w.name)
     line = None
@@ -512,6 +518,9 @@ def run_b200(args):
                          "traffic": traffic, "peak_source": peak_src,
                          "kernel": "pab::decode_kernel", "kernel_us": round(kernel_ms * 1e3, 2),
                          "algorithmic_bytes_per_launch": kv_bytes,
+                         "extra_bytes_per_call": extra_bytes,
+                         "datasheet_peak": DATASHEET_HBM_GBS,
+                         "datasheet_frac": round(achieved / DATASHEET_HBM_GBS, 4),
                          "traffic_source": traffic_src},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
