@@ -298,6 +298,18 @@ typedef struct pab200_kv_append_args {
  * is incremented once per sequence.  One launch, asynchronous on `stream`. */
 int pab200_kv_append(const pab200_kv_append_args* args, void* stream);
 
+/* Append, then decode, in one call: the same as pab200_kv_append(app)
+ * followed by pab200_decode(args) on the same stream, with the append done
+ * by the decode call's planner (one launch fewer per serving step, and it
+ * keeps the planner's overlap with the previous call).  `app` must address
+ * the caches, block table and lengths of `args` (same pointers, layout and
+ * strides; PAB200_ERR_INVALID_ARGUMENT otherwise); its status pointer is
+ * ignored: append bits go to the workspace status word.  The step's
+ * flash-attn-style counterpart is flash_attn_with_kvcache(..., k, v, ...);
+ * the reference wrapper (src/common.py:1-14) has no append. */
+int pab200_decode_append(const pab200_decode_args* args, const pab200_kv_append_args* app,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* Copy the device status word of `workspace` (the PAB200_STATUS_* bits raised
  * by the most recent pab200_decode call on it) to *status_out.  Synchronises
  * `stream`. */

@@ -49,6 +49,7 @@ EXPORTED_SYMBOLS = (
     "pab200_paged_attention",
     "pab200_merge_states",
     "pab200_kv_append",
+    "pab200_decode_append",
     "pab200_exchange_buffer_bytes",
     "pab200_exchange_buffer_create",
     "pab200_exchange_buffer_open",
@@ -169,6 +170,9 @@ def load() -> ctypes.CDLL:
     lib.pab200_paged_attention.restype = ctypes.c_int
     lib.pab200_kv_append.argtypes = [ctypes.POINTER(KvAppendArgs), ctypes.c_void_p]
     lib.pab200_kv_append.restype = ctypes.c_int
+    lib.pab200_decode_append.argtypes = [ctypes.POINTER(DecodeArgs), ctypes.POINTER(KvAppendArgs),
+                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.pab200_decode_append.restype = ctypes.c_int
     lib.pab200_merge_states.argtypes = [
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
         ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,

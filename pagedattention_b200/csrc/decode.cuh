@@ -71,6 +71,24 @@ __host__ __device__ constexpr int core_q_bytes(bool core, int D) {
   return core ? kCoreMaxG * D * 4 : 0;
 }
 
+// Arguments of a KV append (kv_append_kernel, or the planner when a decode
+// call appends its step's token first).
+struct AppendParams {
+  uint32_t* k_cache;
+  uint32_t* v_cache;
+  const uint32_t* k_new;
+  const uint32_t* v_new;
+  int32_t* lens;
+  const int32_t* bt;
+  uint32_t* status;
+  int32_t B, Hkv, D, bs, maxb, head_in_page;  // head_in_page: NHD cache (Hkv rows per token)
+  int64_t num_pages;
+  int64_t n_sb, n_sh, l_sb, l_sh, bt_sb, bt_sh, bt_si;
+  int32_t bt_mul, bt_add, increment;
+};
+
+constexpr uint32_t kStatusAppendFull = 0x10u;
+
 struct DecodeParams {
   void* out;
   const void* q;
@@ -110,6 +128,9 @@ struct DecodeParams {
   // cross-device state output (optional)
   float* state_o;
   float* state_lse;
+  // optional: append each (sequence, kv head)'s new token before planning
+  int32_t append;
+  AppendParams app;
 };
 
 // The warp that owns global page P (0 <= P < T).  Warp w owns pages
@@ -146,8 +167,73 @@ __device__ __forceinline__ __half from_float<__half>(float x) {
 }
 
 // --------------------------------------------------------------------------
+// KV append inside the planner (1024 threads).  Row r = (sequence r / Hkv,
+// kv head r % Hkv): its page and destination row at the current length L, or
+// -1 when there is no slot (L past max_blocks * bs) or the page id is out of
+// range (the status bit is raised by the caller's first pass).
+__device__ __forceinline__ int64_t append_row(const AppendParams& a, int s, int h, int L,
+                                              uint32_t* flags) {
+  if (L < 0) return -1;
+  if (L / a.bs >= a.maxb) {
+    if (flags) *flags |= kStatusAppendFull;
+    return -1;
+  }
+  const int64_t pid =
+      static_cast<int64_t>(a.bt[s * a.bt_sb + h * a.bt_sh + static_cast<int64_t>(L / a.bs) * a.bt_si]) *
+          a.bt_mul + static_cast<int64_t>(h) * a.bt_add;
+  if (pid < 0 || pid >= a.num_pages) {
+    if (flags) *flags |= kStatusBadPage;
+    return -1;
+  }
+  return (pid * a.bs + L % a.bs) * (a.head_in_page ? a.Hkv : 1) + (a.head_in_page ? h : 0);
+}
+
+// Pass 1: warp w of the CTA copies rows w, w + 32, ...; lanes over the
+// row's 32-bit words (head_size 2-byte elements).
+__device__ __forceinline__ void planner_append_rows(const AppendParams& a, int tid) {
+  const int lane = tid & 31, warp = tid >> 5;
+  const int words = a.D / 2;
+  uint32_t flags = 0;
+  for (int r = warp; r < a.B * a.Hkv; r += 32) {
+    const int s = r / a.Hkv, h = r - s * a.Hkv;
+    const int L = a.lens[s * a.l_sb + h * a.l_sh];
+    const int64_t row = append_row(a, s, h, L, &flags);
+    if (row < 0) continue;
+    const int64_t src = (s * a.n_sb + static_cast<int64_t>(h) * a.n_sh) / 2;
+    for (int w = lane; w < words; w += 32) {
+      a.k_cache[row * words + w] = a.k_new[src + w];
+      a.v_cache[row * words + w] = a.v_new[src + w];
+    }
+  }
+  if (flags && lane == 0 && a.status) atomicOr(a.status, flags);
+}
+
+// Pass 2 (after a CTA barrier, so every row read its length first): each
+// written row's length moves to L + 1; a length shared by a sequence's heads
+// moves once, if every head's token was written.
+__device__ __forceinline__ void planner_append_lengths(const AppendParams& a, int tid) {
+  if (!a.increment) return;
+  if (a.l_sh != 0) {
+    for (int r = tid; r < a.B * a.Hkv; r += 1024) {
+      const int s = r / a.Hkv, h = r - s * a.Hkv;
+      int32_t* lp = a.lens + s * a.l_sb + h * a.l_sh;
+      const int L = *lp;
+      if (append_row(a, s, h, L, nullptr) >= 0) *lp = L + 1;
+    }
+  } else {
+    for (int s = tid; s < a.B; s += 1024) {
+      int32_t* lp = a.lens + s * a.l_sb;
+      const int L = *lp;
+      bool ok = true;
+      for (int h = 0; h < a.Hkv; ++h) ok &= append_row(a, s, h, L, nullptr) >= 0;
+      if (ok) *lp = L + 1;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
 // Planner: one CTA of 1024 threads.
-template <typename T>
+template <typename T, bool APPEND>
 __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   __shared__ int32_t warp_tot[32];
   __shared__ uint32_t par_sm;
@@ -165,6 +251,16 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
     *p.n_empty = 0;
     par_sm = (*reinterpret_cast<volatile uint32_t*>(p.parity) ^ 1u) & 1u;
     *p.parity = par_sm;
+  }
+  if constexpr (APPEND) {
+    // The step's new tokens go into the cache first (the previous call's
+    // decode, which read the cache, has completed when this kernel runs):
+    // every row is written at the current length, then the lengths move.
+    __syncthreads();  // status reset before any append bit is raised
+    planner_append_rows(p.app, tid);
+    __syncthreads();
+    planner_append_lengths(p.app, tid);
+    __syncthreads();
   }
   // Thread t owns heads [t * per, (t + 1) * per): its page counts are loaded
   // in one round (up to kPer of them kept in registers), summed, and one
@@ -1402,21 +1498,6 @@ __global__ void __launch_bounds__(256) merge_states_kernel(
 // time with their loads in flight together, into row L % bs of page
 // block_table[L / bs]; last, the lengths move.  A length shared by all heads
 // of a sequence (h stride 0) moves once, if every head's token was written.
-struct AppendParams {
-  uint32_t* k_cache;
-  uint32_t* v_cache;
-  const uint32_t* k_new;
-  const uint32_t* v_new;
-  int32_t* lens;
-  const int32_t* bt;
-  uint32_t* status;
-  int32_t B, Hkv, D, bs, maxb, head_in_page;  // head_in_page: NHD cache (Hkv rows per token)
-  int64_t num_pages;
-  int64_t n_sb, n_sh, l_sb, l_sh, bt_sb, bt_sh, bt_si;
-  int32_t bt_mul, bt_add, increment;
-};
-
-constexpr uint32_t kStatusAppendFull = 0x10u;
 
 __global__ void __launch_bounds__(128) kv_append_kernel(const AppendParams p) {
   const int lane = threadIdx.x & 31;

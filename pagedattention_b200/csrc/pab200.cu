@@ -432,7 +432,8 @@ int encode_cache_map_uncached(const pab200_decode_args* a, const void* base, CUt
 template <typename T>
 cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s, bool pdl) {
   LaunchCfg lc(dim3(1), dim3(1024), 0, s, pdl);
-  return cudaLaunchKernelEx(&lc.cfg, pab::plan_kernel<T>, p);
+  if (p.append) return cudaLaunchKernelEx(&lc.cfg, pab::plan_kernel<T, true>, p);
+  return cudaLaunchKernelEx(&lc.cfg, pab::plan_kernel<T, false>, p);
 }
 
 
@@ -494,8 +495,10 @@ PAB200_EXPORT int pab200_decode_launch_count(const pab200_decode_args* args) {
   return 3;
 }
 
-PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+namespace {
+// One decode call; with `app`, the planner first appends the step's tokens.
+int decode_impl(const pab200_decode_args* a, const pab::AppendParams* app, void* workspace,
+                size_t workspace_bytes, void* stream) {
   Plan pl;
   int rc = make_plan(a, &pl);
   if (rc) return rc;
@@ -549,6 +552,11 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
   p.slot_floats = pl.slot_floats;
   p.state_o = a->state_o;
   p.state_lse = a->state_lse;
+  p.append = app ? 1 : 0;
+  if (app) {
+    p.app = *app;
+    p.app.status = p.status;  // append bits land in the call's status word
+  }
 
   CUtensorMap kmap, vmap;
   if (a->num_pages > 0) {
@@ -581,6 +589,12 @@ PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
                                     : launch_reduce<__half>(p, pl, s, pdl_r);
   if (e != cudaSuccess) return cuda_fail(e, "reduce kernel launch");
   return PAB200_OK;
+}
+}  // namespace
+
+PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return decode_impl(a, nullptr, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------- no-alloc
@@ -819,7 +833,11 @@ PAB200_EXPORT int pab200_exchange_merge(const float* state, void* const* bufs, i
   return PAB200_OK;
 }
 
-PAB200_EXPORT int pab200_kv_append(const pab200_kv_append_args* a, void* stream) {
+namespace {
+// Validates a KV append and fills its kernel parameters.  Returns
+// PAB200_OK, or an error (num_seqs == 0 sets *empty).
+int append_params(const pab200_kv_append_args* a, pab::AppendParams* out, bool* empty) {
+  *empty = false;
   if (!a) return fail(PAB200_ERR_INVALID_ARGUMENT, "args is null");
   if (a->dtype != PAB200_DTYPE_BF16 && a->dtype != PAB200_DTYPE_F16)
     return fail(PAB200_ERR_UNSUPPORTED, "dtype %d: caches must be bf16 or f16", a->dtype);
@@ -829,13 +847,17 @@ PAB200_EXPORT int pab200_kv_append(const pab200_kv_append_args* a, void* stream)
       a->head_size < 2 || (a->head_size & 1) || a->head_size > 256 || a->num_pages < 0)
     return fail(PAB200_ERR_INVALID_ARGUMENT,
                 "need num_seqs >= 0, num_kv_heads, block_size, max_blocks >= 1, even head_size <= 256");
-  if (a->num_seqs == 0) return PAB200_OK;
+  if (a->num_seqs == 0) {
+    *empty = true;
+    return PAB200_OK;
+  }
   if (!a->k_cache || !a->v_cache || !a->k_new || !a->v_new || !a->seqlens || !a->block_table)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
   if (!aligned(a->k_cache, 4) || !aligned(a->v_cache, 4) || !aligned(a->k_new, 4) ||
       !aligned(a->v_new, 4) || (a->new_stride_b & 1) || (a->new_stride_h & 1))
     return fail(PAB200_ERR_ALIGNMENT, "caches and new rows 4-byte aligned, even strides");
-  pab::AppendParams p{};
+  pab::AppendParams& p = *out;
+  p = pab::AppendParams{};
   p.k_cache = static_cast<uint32_t*>(a->k_cache);
   p.v_cache = static_cast<uint32_t*>(a->v_cache);
   p.k_new = static_cast<const uint32_t*>(a->k_new);
@@ -860,9 +882,40 @@ PAB200_EXPORT int pab200_kv_append(const pab200_kv_append_args* a, void* stream)
   p.bt_mul = a->bt_page_mul;
   p.bt_add = a->bt_page_add;
   p.increment = a->increment ? 1 : 0;
+  return PAB200_OK;
+}
+}  // namespace
+
+PAB200_EXPORT int pab200_kv_append(const pab200_kv_append_args* a, void* stream) {
+  pab::AppendParams p;
+  bool empty = false;
+  const int rc = append_params(a, &p, &empty);
+  if (rc || empty) return rc;
   pab::kv_append_kernel<<<(a->num_seqs + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PAB200_OK : cuda_fail(e, "kv append launch");
+}
+
+PAB200_EXPORT int pab200_decode_append(const pab200_decode_args* a, const pab200_kv_append_args* app,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (!a || !app) return fail(PAB200_ERR_INVALID_ARGUMENT, "args is null");
+  pab::AppendParams p;
+  bool empty = false;
+  int rc = append_params(app, &p, &empty);
+  if (rc) return rc;
+  // The append must address the cache, table and lengths this call decodes.
+  if (app->k_cache != a->k_cache || app->v_cache != a->v_cache ||
+      app->block_table != a->block_table || app->seqlens != a->seqlens ||
+      app->dtype != a->dtype || app->layout != a->layout || app->num_seqs != a->num_seqs ||
+      app->num_kv_heads != a->num_kv_heads || app->head_size != a->head_size ||
+      app->block_size != a->block_size || app->max_blocks != a->max_blocks ||
+      app->num_pages != a->num_pages || app->seqlens_stride_b != a->seqlens_stride_b ||
+      app->seqlens_stride_h != a->seqlens_stride_h || app->bt_stride_b != a->bt_stride_b ||
+      app->bt_stride_h != a->bt_stride_h || app->bt_stride_i != a->bt_stride_i ||
+      app->bt_page_mul != a->bt_page_mul || app->bt_page_add != a->bt_page_add)
+    return fail(PAB200_ERR_INVALID_ARGUMENT,
+                "append arguments must name the decode call's caches, block table and lengths");
+  return decode_impl(a, empty ? nullptr : &p, workspace, workspace_bytes, stream);
 }
 
 PAB200_EXPORT int pab200_read_status(const void* workspace, uint32_t* status_out, void* stream) {

@@ -128,17 +128,17 @@ def kernel_events(before: torch.cuda.Event, after: torch.cuda.Event):
         _tls.events = prev
 
 
-def _run_decode(args: _lib.DecodeArgs, device: torch.device) -> None:
+def _run_decode(args: _lib.DecodeArgs, device: torch.device, append=None) -> None:
     lib = _lib.load()
     ev = getattr(_tls, "events", None)
     if ev is not None:
         args.event_before = ev[0].cuda_event
         args.event_after = ev[1].cuda_event
     if torch.cuda.current_device() == device.index:
-        rc = _launch(lib, args, device)
+        rc = _launch(lib, args, device, append)
     else:
         with torch.cuda.device(device):
-            rc = _launch(lib, args, device)
+            rc = _launch(lib, args, device, append)
     if rc == _lib.ERR_INVALID_ARGUMENT or rc == _lib.ERR_UNSUPPORTED:
         raise ValueError(f"pab200_decode: {_lib.error_text(lib, rc)}")
     _lib.check(lib, rc, "pab200_decode")
@@ -153,15 +153,20 @@ def _current_stream_handle(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def _launch(lib, args, device) -> int:
+def _call(lib, args, append, ws, stream_handle) -> int:
+    if append is None:
+        return lib.pab200_decode(ctypes.byref(args), ws.data_ptr(), ws.numel(), stream_handle)
+    return lib.pab200_decode_append(ctypes.byref(args), ctypes.byref(append), ws.data_ptr(),
+                                    ws.numel(), stream_handle)
+
+
+def _launch(lib, args, device, append=None) -> int:
     stream_handle = _current_stream_handle(device)
-    ws = _workspace(lib, args, device, stream_handle)
-    rc = lib.pab200_decode(ctypes.byref(args), ws.data_ptr(), ws.numel(), stream_handle)
+    rc = _call(lib, args, append, _workspace(lib, args, device, stream_handle), stream_handle)
     if rc == _lib.ERR_WORKSPACE:
         # launch geometry changed (e.g. a tuning variable): re-size once
         _ws_sizes.clear()
-        ws = _workspace(lib, args, device, stream_handle)
-        rc = lib.pab200_decode(ctypes.byref(args), ws.data_ptr(), ws.numel(), stream_handle)
+        rc = _call(lib, args, append, _workspace(lib, args, device, stream_handle), stream_handle)
     return rc
 
 
@@ -184,7 +189,7 @@ def _fill_common(args, *, q, k_cache, v_cache, lens, bt, dtype, B, Hq, Hkv, D, b
 
 
 def flash_attn_with_kvcache_wrapper_b200(q, k_cache, v_cache, cache_seqlens, block_table,
-                                         softmax_scale, num_splits=1):
+                                         softmax_scale, num_splits=1, k=None, v=None):
     """Paged decode attention; returns a new (batch, 1, Hq, head_size) tensor.
 
     Arguments as in src/common.py:1-14: q (B, 1, Hq, D); k_cache, v_cache
@@ -193,6 +198,12 @@ def flash_attn_with_kvcache_wrapper_b200(q, k_cache, v_cache, cache_seqlens, blo
     keeps the reference's meaning (src/kernel_triton.py:206-209, chunks per kv
     head): 0 or 1 lets the kernel size the split to the device, n > 1 caps the
     number of chunks at B*Hkv*n.
+
+    ``k``, ``v`` (optional, not in the reference): the step's new token,
+    (B, 1, Hkv, D) or (B, Hkv, D), written into the cache at cache_seqlens
+    before attending (flash-attn's ``flash_attn_with_kvcache`` semantics);
+    cache_seqlens must then be int32 and is advanced in place.  One call,
+    the append done by the decode's planner.
     """
     Hq, Hkv, G, D = _validate_decode_inputs(q, cache_seqlens, block_table)
     _check_dtypes(q, k_cache, v_cache)
@@ -224,7 +235,37 @@ def flash_attn_with_kvcache_wrapper_b200(q, k_cache, v_cache, cache_seqlens, blo
     args.seqlens_stride_b, args.seqlens_stride_h = lens.stride()
     args.bt_stride_b, args.bt_stride_h, args.bt_stride_i = bt.stride()
     args.bt_page_mul, args.bt_page_add = 1, 0
-    _run_decode(args, device)
+    append = None
+    if k is not None or v is not None:
+        if k is None or v is None:
+            raise ValueError("k and v must be given together")
+        if cache_seqlens.dtype != torch.int32:
+            raise TypeError("cache_seqlens must be int32 to be advanced in place")
+        kn = k.reshape(B, Hkv, D) if k.dim() == 4 else k
+        vn = v.reshape(B, Hkv, D) if v.dim() == 4 else v
+        if tuple(kn.shape) != (B, Hkv, D) or tuple(vn.shape) != (B, Hkv, D):
+            raise ValueError("k and v must be (batch, 1, Hkv, head_size) or (batch, Hkv, head_size)")
+        if kn.dtype != k_cache.dtype or vn.dtype != k_cache.dtype:
+            raise TypeError("k and v must have the caches' dtype")
+        if kn.stride(2) != 1 or vn.stride(2) != 1 or kn.stride() != vn.stride():
+            raise ValueError("k and v must share strides, contiguous in head_size")
+        _check_device(q, kn, vn)
+        append = _lib.KvAppendArgs()
+        append.k_cache, append.v_cache = args.k_cache, args.v_cache
+        append.k_new, append.v_new = kn.data_ptr(), vn.data_ptr()
+        append.seqlens, append.block_table = args.seqlens, args.block_table
+        append.dtype, append.layout = args.dtype, args.layout
+        append.num_seqs, append.num_kv_heads = B, Hkv
+        append.head_size, append.block_size = D, args.block_size
+        append.max_blocks, append.num_pages = args.max_blocks, args.num_pages
+        append.new_stride_b, append.new_stride_h = kn.stride(0), kn.stride(1)
+        append.seqlens_stride_b = args.seqlens_stride_b
+        append.seqlens_stride_h = args.seqlens_stride_h
+        append.bt_stride_b, append.bt_stride_h = args.bt_stride_b, args.bt_stride_h
+        append.bt_stride_i = args.bt_stride_i
+        append.bt_page_mul, append.bt_page_add = 1, 0
+        append.increment = 1
+    _run_decode(args, device, append)
     return out
 
 

@@ -185,3 +185,51 @@ def test_decode_after_append(cuda_device):
         kv_append(kd, vd, kn.to(dev), vn.to(dev), ld, btd)
         out = decode(q.to(dev), kd, vd, ld, btd, D ** -0.5)
         assert_close(out, run_oracle(q, k, v, lens, bt, D ** -0.5), what=f"step {step}")
+
+
+def test_decode_append_refuses_mismatched_arguments():
+    """pab200_decode_append checks on the host that the append addresses
+    the decode call's own caches, block table and lengths."""
+    lib = _lib.load()
+    a = _lib.DecodeArgs()
+    a.k_cache = a.v_cache = a.q = a.out = a.seqlens = a.block_table = 4096
+    app = _lib.KvAppendArgs()
+    app.k_cache = app.v_cache = app.k_new = app.v_new = app.seqlens = app.block_table = 4096
+    app.dtype, app.layout = _lib.DTYPE_BF16, _lib.LAYOUT_PAGES
+    app.num_seqs, app.num_kv_heads, app.head_size, app.block_size, app.max_blocks = 2, 2, 128, 16, 4
+    app.num_pages = 64
+    a.num_seqs = 3  # differs
+    assert lib.pab200_decode_append(ctypes.byref(a), ctypes.byref(app), None, 0, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.pab200_decode_append(None, ctypes.byref(app), None, 0, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.gpu
+def test_fused_append_decode_matches_separate_calls(cuda_device):
+    """Three steps of the wrapper with k=, v= (append done by the decode
+    call's planner) against kv_append followed by a plain decode: outputs,
+    caches and lengths are bit-identical, and every step matches the oracle
+    on the appended cache."""
+    from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode, kv_append
+    from tests.util import assert_close, run_oracle
+    B, Hkv, G, D, bs, maxb = 4, 2, 4, 128, 16, 40
+    k, v, _, _, _, bt = _case(B, Hkv, D, bs, maxb, 330, torch.bfloat16, seed=31)
+    lens = torch.tensor([[100, 5], [600, 17], [0, 333], [31, 32]], dtype=torch.int32)
+    dev = cuda_device
+    k1, v1, l1 = k.to(dev), v.to(dev), lens.to(dev)   # fused
+    k2, v2, l2 = k.to(dev), v.to(dev), lens.to(dev)   # separate
+    btd = bt.to(dev)
+    g = torch.Generator().manual_seed(3)
+    for step in range(3):
+        kn = torch.randn((B, 1, Hkv, D), generator=g).to(torch.bfloat16)
+        vn = torch.randn((B, 1, Hkv, D), generator=g).to(torch.bfloat16)
+        q = torch.randn((B, 1, Hkv * G, D), generator=g).to(torch.bfloat16)
+        k, v, lens = _oracle(k, v, kn[:, 0], vn[:, 0], lens, bt)
+        fused = decode(q.to(dev), k1, v1, l1, btd, D ** -0.5, k=kn.to(dev), v=vn.to(dev))
+        kv_append(k2, v2, kn[:, 0].to(dev), vn[:, 0].to(dev), l2, btd)
+        sep = decode(q.to(dev), k2, v2, l2, btd, D ** -0.5)
+        assert torch.equal(fused, sep), f"step {step}"
+        assert torch.equal(k1, k2) and torch.equal(v1, v2) and torch.equal(l1, l2)
+        assert torch.equal(l1.cpu(), lens)
+        assert_close(fused, run_oracle(q, k, v, lens, bt, D ** -0.5), what=f"fused step {step}")
