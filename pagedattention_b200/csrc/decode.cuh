@@ -85,6 +85,7 @@ struct AppendParams {
   int64_t num_pages;
   int64_t n_sb, n_sh, l_sb, l_sh, bt_sb, bt_sh, bt_si;
   int32_t bt_mul, bt_add, increment;
+  int32_t vec16;  // rows copied as 16-byte units (new rows and caches 16-byte aligned)
 };
 
 constexpr uint32_t kStatusAppendFull = 0x10u;
@@ -188,24 +189,45 @@ __device__ __forceinline__ int64_t append_row(const AppendParams& a, int s, int 
   return (pid * a.bs + L % a.bs) * (a.head_in_page ? a.Hkv : 1) + (a.head_in_page ? h : 0);
 }
 
-// Pass 1: warp w of the CTA copies rows w, w + 32, ...; lanes over the
-// row's 32-bit words (head_size 2-byte elements).
+// Pass 1, in chunks of 1024 rows: thread t resolves row t's destination
+// (one round of length and block-table loads), then all 1024 threads copy
+// the chunk's K and V rows in 16-byte units (4-byte words when unaligned).
+// Lengths are not written here, so every row reads its length before any
+// changes.
 __device__ __forceinline__ void planner_append_rows(const AppendParams& a, int tid) {
-  const int lane = tid & 31, warp = tid >> 5;
-  const int words = a.D / 2;
+  __shared__ int64_t dst[1024];
+  __shared__ int64_t src_sm[1024];
+  const int rows = a.B * a.Hkv;
+  const int unit_words = a.vec16 ? 4 : 1;
+  const int units = a.D / 2 / unit_words;  // per row
   uint32_t flags = 0;
-  for (int r = warp; r < a.B * a.Hkv; r += 32) {
-    const int s = r / a.Hkv, h = r - s * a.Hkv;
-    const int L = a.lens[s * a.l_sb + h * a.l_sh];
-    const int64_t row = append_row(a, s, h, L, &flags);
-    if (row < 0) continue;
-    const int64_t src = (s * a.n_sb + static_cast<int64_t>(h) * a.n_sh) / 2;
-    for (int w = lane; w < words; w += 32) {
-      a.k_cache[row * words + w] = a.k_new[src + w];
-      a.v_cache[row * words + w] = a.v_new[src + w];
+  for (int c0 = 0; c0 < rows; c0 += 1024) {
+    const int r = c0 + tid;
+    if (r < rows) {
+      const int s = r / a.Hkv, h = r - s * a.Hkv;
+      const int L = a.lens[s * a.l_sb + h * a.l_sh];
+      dst[tid] = append_row(a, s, h, L, &flags);
+      src_sm[tid] = (s * a.n_sb + static_cast<int64_t>(h) * a.n_sh) / 2;
     }
+    __syncthreads();
+    const int n = min(1024, rows - c0);
+    for (int u = tid; u < n * units; u += 1024) {
+      const int rr = u / units, part = u - rr * units;
+      const int64_t row = dst[rr];
+      if (row < 0) continue;
+      const int64_t so = src_sm[rr] + part * unit_words;
+      const int64_t doff = row * (a.D / 2) + part * unit_words;
+      if (a.vec16) {
+        *reinterpret_cast<uint4*>(a.k_cache + doff) = *reinterpret_cast<const uint4*>(a.k_new + so);
+        *reinterpret_cast<uint4*>(a.v_cache + doff) = *reinterpret_cast<const uint4*>(a.v_new + so);
+      } else {
+        a.k_cache[doff] = a.k_new[so];
+        a.v_cache[doff] = a.v_new[so];
+      }
+    }
+    __syncthreads();  // dst / src_sm are reused by the next chunk
   }
-  if (flags && lane == 0 && a.status) atomicOr(a.status, flags);
+  if (flags && a.status) atomicOr(a.status, flags);
 }
 
 // Pass 2 (after a CTA barrier, so every row read its length first): each

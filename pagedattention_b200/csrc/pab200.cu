@@ -882,6 +882,10 @@ int append_params(const pab200_kv_append_args* a, pab::AppendParams* out, bool* 
   p.bt_mul = a->bt_page_mul;
   p.bt_add = a->bt_page_add;
   p.increment = a->increment ? 1 : 0;
+  // 16-byte row copies when every row start is 16-byte aligned
+  p.vec16 = aligned(a->k_cache, 16) && aligned(a->v_cache, 16) && aligned(a->k_new, 16) &&
+            aligned(a->v_new, 16) && (a->new_stride_b % 8 == 0) && (a->new_stride_h % 8 == 0) &&
+            (a->head_size % 8 == 0);
   return PAB200_OK;
 }
 }  // namespace
