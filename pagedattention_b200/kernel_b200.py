@@ -340,8 +340,32 @@ def _paged_args(query, key_cache, value_cache, block_tables, context_lens, scale
     return args, device, (bt, lens)
 
 
+def _append_args_like(args, k_new, v_new, lens):
+    """KvAppendArgs addressing the caches, table and lengths of ``args``."""
+    B, Hkv, D = args.num_seqs, args.num_kv_heads, args.head_size
+    if tuple(k_new.shape) != (B, Hkv, D) or tuple(v_new.shape) != (B, Hkv, D):
+        raise ValueError("k_new and v_new must be (num_seqs, num_kv_heads, head_size)")
+    if k_new.stride(2) != 1 or v_new.stride(2) != 1 or k_new.stride() != v_new.stride():
+        raise ValueError("k_new and v_new must share strides, contiguous in head_size")
+    if lens.dtype != torch.int32:
+        raise TypeError("context_lens must be int32 to be advanced in place")
+    a = _lib.KvAppendArgs()
+    a.k_cache, a.v_cache = args.k_cache, args.v_cache
+    a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
+    a.seqlens, a.block_table = args.seqlens, args.block_table
+    a.dtype, a.layout = args.dtype, args.layout
+    a.num_seqs, a.num_kv_heads, a.head_size = B, Hkv, D
+    a.block_size, a.max_blocks, a.num_pages = args.block_size, args.max_blocks, args.num_pages
+    a.new_stride_b, a.new_stride_h = k_new.stride(0), k_new.stride(1)
+    a.seqlens_stride_b, a.seqlens_stride_h = args.seqlens_stride_b, args.seqlens_stride_h
+    a.bt_stride_b, a.bt_stride_h, a.bt_stride_i = args.bt_stride_b, args.bt_stride_h, args.bt_stride_i
+    a.bt_page_mul, a.bt_page_add = args.bt_page_mul, args.bt_page_add
+    a.increment = 1
+    return a
+
+
 def paged_attention(out, query, key_cache, value_cache, block_tables, context_lens, scale,
-                    block_size, kv_layout="HND", num_splits=0):
+                    block_size, kv_layout="HND", num_splits=0, k_new=None, v_new=None):
     """In-place paged decode: writes ``out`` (num_seqs, num_q_heads, head_size).
 
     Caches: (num_pages, block_size, head_size) with block_tables
@@ -349,7 +373,10 @@ def paged_attention(out, query, key_cache, value_cache, block_tables, context_le
     (num_blocks, num_kv_heads, block_size, head_size) ("HND", default) or
     (num_blocks, block_size, num_kv_heads, head_size) ("NHD") with block_tables
     (num_seqs, max_blocks) of block ids shared by all kv heads.  context_lens:
-    (num_seqs,) or (num_seqs, num_kv_heads).
+    (num_seqs,) or (num_seqs, num_kv_heads).  With ``k_new``, ``v_new``
+    (num_seqs, num_kv_heads, head_size) the step's tokens are first written
+    at the current lengths, which advance in place (int32 context_lens),
+    inside the same call.
     """
     args, device, keep = _paged_args(query, key_cache, value_cache, block_tables, context_lens,
                                      scale, block_size, kv_layout, num_splits)
@@ -359,7 +386,15 @@ def paged_attention(out, query, key_cache, value_cache, block_tables, context_le
         raise ValueError("out must be contiguous in head_size")
     args.out = out.data_ptr()
     args.out_stride_b, args.out_stride_h = out.stride(0), out.stride(1)
-    _run_decode(args, device)
+    append = None
+    if k_new is not None or v_new is not None:
+        if k_new is None or v_new is None:
+            raise ValueError("k_new and v_new must be given together")
+        if k_new.dtype != key_cache.dtype or v_new.dtype != key_cache.dtype:
+            raise TypeError("k_new and v_new must have the caches' dtype")
+        _check_device(query, k_new, v_new)
+        append = _append_args_like(args, k_new, v_new, context_lens)
+    _run_decode(args, device, append)
     del keep
 
 

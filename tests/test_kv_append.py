@@ -233,3 +233,32 @@ def test_fused_append_decode_matches_separate_calls(cuda_device):
         assert torch.equal(k1, k2) and torch.equal(v1, v2) and torch.equal(l1, l2)
         assert torch.equal(l1.cpu(), lens)
         assert_close(fused, run_oracle(q, k, v, lens, bt, D ** -0.5), what=f"fused step {step}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layout", ["HND", "NHD"])
+def test_fused_append_paged_attention_pools(cuda_device, layout):
+    """paged_attention(..., k_new=, v_new=) over a vLLM-style pool with
+    per-sequence lengths equals kv_append followed by paged_attention."""
+    from pagedattention_b200 import kv_append, paged_attention
+    B, Hkv, G, D, bs, maxb, nb = 5, 4, 4, 128, 16, 6, 40
+    g = torch.Generator().manual_seed(8)
+    shape = (nb, Hkv, bs, D) if layout == "HND" else (nb, bs, Hkv, D)
+    pk = torch.randn(shape, generator=g).to(torch.bfloat16)
+    pv = torch.randn(shape, generator=g).to(torch.bfloat16)
+    bt = torch.randperm(nb, generator=g)[:B * maxb].to(torch.int32).reshape(B, maxb)
+    lens = torch.randint(0, maxb * bs - 2, (B,), generator=g, dtype=torch.int32)
+    dev = cuda_device
+    k1, v1, l1 = pk.to(dev), pv.to(dev), lens.to(dev)
+    k2, v2, l2 = pk.to(dev), pv.to(dev), lens.to(dev)
+    btd = bt.to(dev)
+    for step in range(2):
+        kn = torch.randn((B, Hkv, D), generator=g).to(torch.bfloat16).to(dev)
+        vn = torch.randn((B, Hkv, D), generator=g).to(torch.bfloat16).to(dev)
+        q = torch.randn((B, Hkv * G, D), generator=g).to(torch.bfloat16).to(dev)
+        o1, o2 = torch.empty_like(q), torch.empty_like(q)
+        paged_attention(o1, q, k1, v1, btd, l1, D ** -0.5, bs, kv_layout=layout, k_new=kn, v_new=vn)
+        kv_append(k2, v2, kn, vn, l2, btd, kv_layout=layout)
+        paged_attention(o2, q, k2, v2, btd, l2, D ** -0.5, bs, kv_layout=layout)
+        assert torch.equal(o1, o2) and torch.equal(k1, k2) and torch.equal(v1, v2)
+        assert torch.equal(l1, l2) and torch.equal(l1.cpu(), lens + step + 1)
