@@ -248,7 +248,8 @@ def run_b200(args):
 
     from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode
     from pagedattention_b200.distributed import (PeerExchange, context_ranges,
-                                                 decode_context_parallel, shard_sequences)
+                                                 decode_context_parallel, lens_of_units,
+                                                 shard_heads, shard_sequences)
     from pagedattention_b200.kernel_b200 import kernel_events, launches_per_call
     from pagedattention_b200.workloads import WORKLOADS, make_inputs, sample_lens
 
@@ -281,11 +282,17 @@ def run_b200(args):
     if mode == "replicate":      # every rank decodes its own batch
         inp = make_inputs(w, seed=args.seed + rank, device=dev, gen_device=dev)
         parallelism = f"dp{world} (independent sequence batches per rank, no collective)"
-    elif mode == "shard":        # one batch, sequences split over ranks (LPT by tokens)
+    elif mode == "shard" and len(lens_all) >= world:  # sequences split over ranks (LPT)
         idx = shard_sequences(lens_all.tolist(), world)[rank]
         inp = make_inputs(w, seed=args.seed + rank, device=dev, gen_device=dev,
                           lens=lens_all[idx])
         parallelism = f"sequence-sharded over {world} ranks (LPT by tokens), no collective"
+    elif mode == "shard":        # fewer sequences than ranks: (sequence, kv head) units
+        inp = make_inputs(w, seed=args.seed, device=dev, gen_device=dev, lens=lens_all)
+        lens2d = lens_all[:, None].expand(len(lens_all), w.num_kv_heads)
+        head_units = shard_heads(lens2d, world)[rank]
+        parallelism = (f"(sequence, kv head)-sharded over {world} ranks (LPT by tokens), "
+                       "no collective")
     else:                        # every context split over ranks, states merged over NCCL
         starts, ends = context_ranges(lens_all, world, w.partition_tokens or 512)
         inp = make_inputs(w, seed=args.seed, device=dev, gen_device=dev,
@@ -298,6 +305,9 @@ def run_b200(args):
     q, k, v, sl, bt = inp.reference_layout()
     bt = bt.contiguous()
     kv_bytes = inp.kv_bytes()
+    if mode == "shard" and len(lens_all) < world:
+        sl = lens_of_units(sl.cpu(), head_units).to(torch.int32).to(dev)
+        kv_bytes = int(sl.to(torch.int64).sum()) * w.head_size * elt * 2
     total_bytes = kv_bytes * world if mode == "replicate" else global_bytes
     L2 = torch.cuda.get_device_properties(dev).L2_cache_size
     # Keep every step's KV out of L2: workloads whose KV is under 3x L2

@@ -5,7 +5,9 @@ The decode path spreads over devices in two ways:
 * Sequence sharding — no collective.  Sequences are independent, so each rank
   decodes its own; ``shard_sequences`` balances ranks by tokens
   (longest-processing-time-first), since KV bytes, not sequence count, set
-  the time.
+  the time.  With fewer sequences than ranks, ``shard_heads`` splits by
+  (sequence, kv head) instead and ``lens_of_units`` gives a rank the
+  lengths of its units only.
 * Context split — one exchange.  A context too long for one device's share
   is cut into contiguous token ranges, one per rank (``context_ranges``).
   Each rank decodes its range of every sequence into a packed (o, lse) state
@@ -47,6 +49,33 @@ def shard_sequences(lens, world_size: int) -> list[list[int]]:
         shards[r].append(i)
         heapq.heappush(heap, (load + lens[i], r))
     return [sorted(s) for s in shards]
+
+
+def shard_heads(lens, world_size: int) -> list[list[tuple[int, int]]]:
+    """Assign (sequence, kv head) units to ranks, balancing tokens (LPT, as
+    ``shard_sequences``) — for batches with fewer sequences than ranks.
+    ``lens``: (num_seqs, num_kv_heads) lengths.  Every rank's list is sorted."""
+    lens = torch.as_tensor(lens)
+    B, Hkv = lens.shape
+    flat = [int(x) for x in lens.reshape(-1).tolist()]
+    heap = [(0, r) for r in range(world_size)]
+    shards = [[] for _ in range(world_size)]
+    for i in sorted(range(len(flat)), key=lambda i: (-flat[i], i)):
+        load, r = heapq.heappop(heap)
+        shards[r].append(divmod(i, Hkv))
+        heapq.heappush(heap, (load + flat[i], r))
+    return [sorted(s) for s in shards]
+
+
+def lens_of_units(lens, units):
+    """Per-(sequence, kv head) lengths of a rank that owns ``units``: the
+    others become 0 (an empty head: no pages read, a zero output row that the
+    owning rank overwrites in its own result)."""
+    lens = torch.as_tensor(lens)
+    out = torch.zeros_like(lens)
+    for s, h in units:
+        out[s, h] = lens[s, h]
+    return out
 
 
 def context_ranges(lens, world_size: int, align: int):

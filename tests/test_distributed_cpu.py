@@ -110,3 +110,16 @@ def test_context_split_gather_merge_two_gloo_ranks():
     assert all(p.exitcode == 0 for p in procs)
     res = dict(q.get(timeout=5) for _ in range(2))
     assert max(res.values()) < 1e-4, res
+
+
+def test_shard_heads_covers_every_unit_and_balances():
+    from pagedattention_b200.distributed import lens_of_units, shard_heads
+    lens = torch.tensor([[32768, 30000, 100, 5], [65536, 0, 7, 900]])
+    shards = shard_heads(lens, 4)
+    units = sorted(u for sh in shards for u in sh)
+    assert units == [(s, h) for s in range(2) for h in range(4)]
+    loads = [sum(int(lens[s, h]) for s, h in sh) for sh in shards]
+    assert max(loads) - min(loads) <= int(lens.max())
+    total = sum(lens_of_units(lens, sh) for sh in shards)
+    assert torch.equal(total, lens)
+    assert int(lens_of_units(lens, shards[0]).count_nonzero()) <= len(shards[0])

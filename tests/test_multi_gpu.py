@@ -29,8 +29,8 @@ def _worker(rank, world, port, q):
 
     from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode
     from pagedattention_b200.distributed import (PeerExchange, context_ranges,
-                                                 decode_context_parallel, local_view,
-                                                 shard_sequences)
+                                                 decode_context_parallel, lens_of_units,
+                                                 local_view, shard_heads, shard_sequences)
     from pagedattention_b200.workloads import WORKLOADS, make_inputs
     from tests.util import ATOL, RTOL, run_oracle
 
@@ -74,7 +74,20 @@ def _worker(rank, world, port, q):
                       inp.scale)
         ref = run_oracle(q4[idx], kp, vp, sl[idx], bt[idx], inp.scale)
         ok_shard = bool(torch.isclose(mine.float().cpu(), ref, atol=ATOL, rtol=RTOL).all())
-        q.put((rank, ok_split, ok_shard))
+        # 3) fewer sequences than ranks: (sequence, kv head) units; every rank
+        #    decodes the batch with only its units' lengths and owns those rows
+        w = WORKLOADS["llama8b_gqa"]
+        inp = make_inputs(w, seed=9, lens=torch.tensor([3000], dtype=torch.int32))
+        q4, kp, vp, sl, bt = inp.reference_layout()
+        units = shard_heads(sl, world)[rank]
+        outh = decode(q4.to(dev), kp.to(dev), vp.to(dev), lens_of_units(sl, units).to(dev),
+                      bt.to(dev), inp.scale).float().cpu()
+        ref = run_oracle(q4, kp, vp, sl, bt, inp.scale)
+        G = q4.shape[2] // sl.shape[1]
+        ok_heads = len(units) > 0 and all(
+            bool(torch.isclose(outh[s, 0, h * G:(h + 1) * G], ref[s, 0, h * G:(h + 1) * G],
+                               atol=ATOL, rtol=RTOL).all()) for s, h in units)
+        q.put((rank, ok_split, ok_shard and ok_heads))
     finally:
         dist.destroy_process_group()
 
