@@ -100,7 +100,8 @@ typedef struct pab200_decode_args {
   int32_t dtype;             /* pab200_dtype (BF16 or F16)                   */
   int32_t layout;            /* pab200_layout                                */
   int32_t num_seqs;          /* B                                            */
-  int32_t num_q_heads;       /* Hq                                           */
+  int32_t num_q_heads;       /* Hq; G = Hq/Hkv with G*D <= 2048, or G <= 32
+                                at D <= 128                                  */
   int32_t num_kv_heads;      /* Hkv                                          */
   int32_t head_size;         /* D: 64, 128 or 256                            */
   int32_t block_size;        /* tokens per page: 8, 16, 32 or 64             */

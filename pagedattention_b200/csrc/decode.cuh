@@ -544,8 +544,17 @@ __device__ __forceinline__ void write_row(const DecodeParams& p, int hd, int g, 
 // >= block_size).  CORE selects CUDA-core arithmetic instead of tensor-core
 // MMA for small query groups (G <= kCoreMaxG, ST == 32): one token per lane
 // for q.K, a warp-shuffle softmax, lanes over the head dimension for P.V.
-template <typename T, int D, int NT, int ST, bool CORE>
-__global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
+// PAIR splits a large query group over two warps that share one ring: the
+// even warp of a pair (the leader) schedules, claims and issues every stage
+// and computes query heads [0, 8 NT); the odd warp follows the stage records
+// the leader writes, computes heads [8 NT, 16 NT), and releases each slot
+// through a second mbarrier before the leader refills it (a sentinel record
+// ends its loop).  Half the accumulator per warp halves the registers, so a
+// group of up to 32 query heads fits at D = 128.  (At D = 64 the pair runs
+// twice the resident warps of the single-warp kernel but is slower: each
+// stage waits on both warps, and the per-stage issue work does not split.)
+template <typename T, int D, int NT, int ST, bool CORE, bool PAIR = false>
+__global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 1)
     decode_kernel(const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap,
                   const DecodeParams p) {
@@ -561,6 +570,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   static_assert(!CORE || (ST == 32 && NT == 1 && D <= 128), "CUDA-core path shape");
   constexpr int DL = D / 32;  // head-dim elements per lane (CUDA-core path)
   static_assert(NH == 1 || NH == 2 || NH == 4, "head size");
+  static_assert(!(CORE && PAIR), "the CUDA-core path has no paired variant");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -571,7 +581,13 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int warp = threadIdx.x >> 5;
   const int wpc = blockDim.x >> 5;
   const int depth = p.depth;
-  const int gw = blockIdx.x * wpc + warp;
+  // A "unit" owns one ring and one page range: a warp, or a pair of warps
+  // (wpc is even for PAIR).  role 1 is the follower of a pair.
+  const int role = PAIR ? (warp & 1) : 0;
+  const int unit = PAIR ? (warp >> 1) : warp;
+  const int upc = PAIR ? (wpc >> 1) : wpc;
+  const int gw = blockIdx.x * upc + unit;
+  const int g_lo = PAIR ? role * NT * 8 : 0;  // first query head of this warp
   // Everything below reads what the planner wrote.  The start-up values are
   // independent loads, issued together (wstart has total_warps entries, so
   // the read is in bounds even for a warp that then exits).
@@ -589,7 +605,8 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     const int hd = p.empty[e];
     const int s = hd / p.Hkv, h = hd - s * p.Hkv;
     const int Hq = p.Hkv * p.G;
-    for (int g = 0; g < p.G; ++g) {
+    const int g_hi = PAIR ? min(p.G, g_lo + NT * 8) : p.G;
+    for (int g = g_lo; g < g_hi; ++g) {
       const int qh = h * p.G + g;
       for (int c = lane * 4; c < D; c += 128) {
         if (p.state_o)
@@ -623,21 +640,39 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   const int log2_pps = LOG2_ST - log2_bs;     // pages per stage = ST / bs
   const int pps = 1 << log2_pps;
   const int cap = p.maxb << log2_bs;
-  const uint32_t ring = smem_base + warp * depth * STAGE_BYTES;
-  uint8_t* tail = smem + wpc * depth * STAGE_BYTES;
-  const uint32_t bars = smem_addr(tail) + warp * kMaxDepth * 8;
-  int4* meta = reinterpret_cast<int4*>(tail + wpc * kMaxDepth * 8) +
-               warp * kMaxDepth * 2;
-  float* qsm = reinterpret_cast<float*>(tail + wpc * kMaxDepth * (8 + kMetaBytesPerSlot)) +
-               warp * (core_q_bytes(CORE, D) / 4);
+  const uint32_t ring = smem_base + unit * depth * STAGE_BYTES;
+  uint8_t* tail = smem + upc * depth * STAGE_BYTES;
+  const uint32_t bars = smem_addr(tail) + unit * kMaxDepth * 8;
+  int4* meta = reinterpret_cast<int4*>(tail + upc * kMaxDepth * 8) +
+               unit * kMaxDepth * 2;
+  float* qsm = reinterpret_cast<float*>(tail + upc * kMaxDepth * (8 + kMetaBytesPerSlot)) +
+               unit * (core_q_bytes(CORE, D) / 4);
+  // PAIR: "slot free" barriers, one arrival (the follower's) per phase.
+  const uint32_t empties = smem_addr(tail) + upc * kMaxDepth * (8 + kMetaBytesPerSlot) +
+                           upc * core_q_bytes(CORE, D) + unit * kMaxDepth * 8;
 
-  if (lane == 0) {
-    for (int i = 0; i < depth; ++i) mbar_init(bars + i * 8, 1);
+  if (lane == 0 && role == 0) {
+    for (int i = 0; i < depth; ++i) {
+      mbar_init(bars + i * 8, 1);
+      if constexpr (PAIR) mbar_init(empties + i * 8, 1);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
-  __syncwarp();
+  if constexpr (PAIR) {
+    // The pair's barriers are initialised.  Fixed barrier ids (one per
+    // ring; upc <= kMaxWarpsPerCta / 2 = 4) keep the count ptxas reserves low.
+    static_assert(kMaxWarpsPerCta / 2 <= 4, "one named barrier per ring");
+    switch (unit) {
+      case 0: named_barrier_sync<1>(64); break;
+      case 1: named_barrier_sync<2>(64); break;
+      case 2: named_barrier_sync<3>(64); break;
+      default: named_barrier_sync<4>(64); break;
+    }
+  } else {
+    __syncwarp();
+  }
   const uint64_t policy = l2_policy_evict_first();
 
   // ------------------------------------------------ issue-side cursor state
@@ -879,7 +914,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
     } else {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int g = nt * 8 + lr;
+      const int g = g_lo + nt * 8 + lr;
       if (load_q) {
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
@@ -982,7 +1017,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int g = nt * 8 + lc * 2 + (i & 1);
+            const int g = g_lo + nt * 8 + lc * 2 + (i & 1);
             const int d = dt * 16 + lr + (i >> 1) * 8;
             if (g < G) {
               const float v = acc[dt][nt][i] * inv[nt][i & 1];
@@ -998,7 +1033,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int g = nt * 8 + lc * 2 + e;
+            const int g = g_lo + nt * 8 + lc * 2 + e;
             if (g < G)
               p.state_lse[static_cast<int64_t>(s) * Hq + h * G + g] =
                   (mrun[nt][e] + __log2f(lt[nt][e])) * kLn2;
@@ -1014,7 +1049,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int g = nt * 8 + lc * 2 + (i & 1);
+          const int g = g_lo + nt * 8 + lc * 2 + (i & 1);
           const int d = dt * 16 + lr + (i >> 1) * 8;
           if (g < G) __stcg(ps + g * D + d, acc[dt][nt][i]);
         }
@@ -1023,7 +1058,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int g = nt * 8 + lc * 2 + e;
+          const int g = g_lo + nt * 8 + lc * 2 + e;
           if (g < G) {
             __stcg(ps + G * D + g, mrun[nt][e]);
             __stcg(ps + G * D + G + g, lt[nt][e]);
@@ -1034,19 +1069,42 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
   };
 
   // ------------------------------------------------ pipeline
-  prepare_next();
-  int issued = 0;
-  for (int i = 0; i < depth; ++i) {
-    if (!issue(i)) break;
-    ++issued;
+  int issued = 0;          // stages issued (leader)
+  bool sent_end = false;   // PAIR leader: the follower's end record is out
+  // PAIR: the record of stage `issued` in (free) slot `slot` says "no more
+  // stages"; a plain arrival completes the slot's phase.
+  auto send_end = [&](int slot) {
+    if (lane == 0) {
+      meta[slot * 2] = make_int4(-1, 0, 0, 0);
+      mbar_arrive(bars + slot * 8);
+    }
+    sent_end = true;
+  };
+  if (role == 0) {
+    prepare_next();
+    for (int i = 0; i < depth; ++i) {
+      if (!issue(i)) {
+        if constexpr (PAIR) send_end(i);
+        break;
+      }
+      ++issued;
+    }
   }
 
   // Accumulation in progress: head, segment, the head's segment range.
   int cur_head = -1, cur_slot = -1, cur_vfirst = 0, cur_vlast = 0;
-  for (int it = 0; it < issued; ++it) {
+  // The leader consumes the stages it issued; the follower runs until the
+  // end record (every wait is bounded).
+  for (int it = 0; role != 0 || it < issued; ++it) {
     const int slot = it % depth;
+    const uint32_t par = static_cast<uint32_t>((it / depth) & 1);
+    if (role != 0 && !mbar_wait(bars + slot * 8, par, kWaitLimitNs)) {
+      if (lane == 0) atomicOr(p.status, kStatusTimeout);
+      return;  // the leader's copies are the leader's to wait for
+    }
     const int4 m0 = meta[slot * 2];
     const int4 m1 = meta[slot * 2 + 1];
+    if (PAIR && m0.x < 0) break;  // end record (follower)
     if (m0.x != cur_head || m1.x != cur_slot) {
       if (cur_head >= 0) finish_head(cur_head, cur_slot, cur_vfirst, cur_vlast);
       const bool new_head = m0.x != cur_head;
@@ -1056,8 +1114,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       cur_vlast = m1.w;
       start_head(cur_head, new_head);
     }
-    const uint32_t bar = bars + slot * 8;
-    if (!mbar_wait(bar, static_cast<uint32_t>((it / depth) & 1), kWaitLimitNs)) {
+    if (role == 0 && !mbar_wait(bars + slot * 8, par, kWaitLimitNs)) {
       if (lane == 0) atomicOr(p.status, kStatusTimeout);
       for (int j = it + 1; j < issued; ++j)
         mbar_wait(bars + (j % depth) * 8, static_cast<uint32_t>((j / depth) & 1),
@@ -1274,7 +1331,27 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, 1)
       fence_proxy_async_smem();
       __syncwarp();
     }
-    if (issue(slot)) ++issued;
+    if constexpr (PAIR) {
+      if (role != 0) {  // the follower is done with the slot
+        if (lane == 0) mbar_arrive(empties + slot * 8);
+        continue;
+      }
+      if (sent_end) continue;
+      // Refill only once the follower has released the slot (stage it).
+      if (!mbar_wait(empties + slot * 8, par, kWaitLimitNs)) {
+        if (lane == 0) atomicOr(p.status, kStatusTimeout);
+        for (int j = it + 1; j < issued; ++j)
+          mbar_wait(bars + (j % depth) * 8, static_cast<uint32_t>((j / depth) & 1),
+                    kWaitLimitNs);
+        return;
+      }
+      if (issue(slot))
+        ++issued;
+      else
+        send_end(slot);
+    } else {
+      if (issue(slot)) ++issued;
+    }
   }
   if (cur_head >= 0) finish_head(cur_head, cur_slot, cur_vfirst, cur_vlast);
 }

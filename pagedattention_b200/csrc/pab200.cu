@@ -97,22 +97,30 @@ struct LaunchCfg {
   }
 };
 
-template <typename T, int D, int NT, int ST, bool CORE>
+template <typename T, int D, int NT, int ST, bool CORE, bool PAIR>
 cudaError_t launch_decode(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
                           const CUtensorMap& k, const CUtensorMap& v,
                           const pab::DecodeParams& p) {
   LaunchCfg lc(grid, block, smem, s, pdl);
-  return cudaLaunchKernelEx(&lc.cfg, pab::decode_kernel<T, D, NT, ST, CORE>, k, v, p);
+  return cudaLaunchKernelEx(&lc.cfg, pab::decode_kernel<T, D, NT, ST, CORE, PAIR>, k, v, p);
 }
 
-template <typename T, int D, int NT, int ST, bool CORE = false>
+template <typename T, int D, int NT, int ST, bool CORE = false, bool PAIR = false>
 KernelOps ops_of() {
-  return KernelOps{reinterpret_cast<void*>(&pab::decode_kernel<T, D, NT, ST, CORE>),
-                   &launch_decode<T, D, NT, ST, CORE>};
+  return KernelOps{reinterpret_cast<void*>(&pab::decode_kernel<T, D, NT, ST, CORE, PAIR>),
+                   &launch_decode<T, D, NT, ST, CORE, PAIR>};
 }
 
 template <typename T, int ST>
-bool select_dnt(int D, int nt, bool core, KernelOps* o) {
+bool select_dnt(int D, int nt, bool core, bool pair, KernelOps* o) {
+  if (pair) {  // two warps per ring, 16 query heads each
+    if (nt != 2) return false;
+    switch (D) {
+      case 64: *o = ops_of<T, 64, 2, ST, false, true>(); return true;
+      case 128: *o = ops_of<T, 128, 2, ST, false, true>(); return true;
+      default: return false;
+    }
+  }
   if (core) {  // CUDA-core path: G <= 4, 32-token stages, D <= 128
     if (ST != 32 || nt != 1) return false;
     switch (D) {
@@ -132,19 +140,19 @@ bool select_dnt(int D, int nt, bool core, KernelOps* o) {
   }
 }
 
-bool select_kernel(int dtype, int D, int nt, int st, bool core, KernelOps* o) {
+bool select_kernel(int dtype, int D, int nt, int st, bool core, bool pair, KernelOps* o) {
   if (dtype == PAB200_DTYPE_BF16) {
     switch (st) {
-      case 16: return select_dnt<__nv_bfloat16, 16>(D, nt, core, o);
-      case 32: return select_dnt<__nv_bfloat16, 32>(D, nt, core, o);
-      case 64: return select_dnt<__nv_bfloat16, 64>(D, nt, core, o);
+      case 16: return select_dnt<__nv_bfloat16, 16>(D, nt, core, pair, o);
+      case 32: return select_dnt<__nv_bfloat16, 32>(D, nt, core, pair, o);
+      case 64: return select_dnt<__nv_bfloat16, 64>(D, nt, core, pair, o);
       default: return false;
     }
   }
   switch (st) {
-    case 16: return select_dnt<__half, 16>(D, nt, core, o);
-    case 32: return select_dnt<__half, 32>(D, nt, core, o);
-    case 64: return select_dnt<__half, 64>(D, nt, core, o);
+    case 16: return select_dnt<__half, 16>(D, nt, core, pair, o);
+    case 32: return select_dnt<__half, 32>(D, nt, core, pair, o);
+    case 64: return select_dnt<__half, 64>(D, nt, core, pair, o);
     default: return false;
   }
 }
@@ -153,7 +161,7 @@ bool select_kernel(int dtype, int D, int nt, int st, bool core, KernelOps* o) {
 struct Plan {
   KernelOps ops;
   int G, nt, st, wpc, depth, ctas_per_sm, grid, W;
-  bool core;
+  bool core, pair;
   size_t smem;
   int n_heads;
   int slot_floats;
@@ -184,9 +192,12 @@ int validate(const pab200_decode_args* a) {
   if (bs != 8 && bs != 16 && bs != 32 && bs != 64)
     return fail(PAB200_ERR_UNSUPPORTED, "block_size %d: supported 8, 16, 32, 64", bs);
   const int G = a->num_q_heads / a->num_kv_heads;
-  if (G * D > 2048)
+  // One warp holds at most 16 query heads x 128 (or 8 x 256) accumulators;
+  // groups of 17-32 heads at D <= 128 are split over a pair of warps.
+  if (G * D > 2048 && !(G <= 32 && D <= 128))
     return fail(PAB200_ERR_UNSUPPORTED,
-                "query group %d x head_size %d exceeds the register tile (G*D <= 2048)", G, D);
+                "query group %d x head_size %d exceeds the register tile "
+                "(G*D <= 2048, or G <= 32 with head_size <= 128)", G, D);
   if (a->max_blocks < 0 || a->num_pages < 0)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "max_blocks and num_pages must be >= 0");
   const int64_t n_heads = int64_t(a->num_seqs) * a->num_kv_heads;
@@ -217,9 +228,12 @@ int validate(const pab200_decode_args* a) {
 
 // Dynamic shared memory of one decode CTA: ring slots, then per-warp
 // mbarriers, stage records and merge scratch (see decode_kernel).
-size_t decode_smem(int wpc, int depth, size_t stage, int nt, int core_bytes) {
-  return 1024 + size_t(wpc) * depth * stage +
-         size_t(wpc) * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + core_bytes);
+// A paired kernel has one ring (and a second set of mbarriers) per two warps.
+size_t decode_smem(int wpc, int depth, size_t stage, bool pair, int core_bytes) {
+  const size_t units = pair ? size_t(wpc / 2) : size_t(wpc);
+  return 1024 + units * depth * stage +
+         units * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + core_bytes) +
+         (pair ? units * pab::kMaxDepth * 8 : 0);
 }
 
 struct Geometry {
@@ -232,8 +246,8 @@ struct Geometry {
 // try every CTA size and keep the one with the most warps per SM (shared
 // memory and registers both limit it; ties go to the larger CTA).  Results
 // are cached per device, kernel, ring depth and stage size.
-int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, int nt, int core_bytes,
-                    int forced_wpc, Geometry* out) {
+int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, bool pair,
+                    int core_bytes, int forced_wpc, Geometry* out) {
   struct Entry {
     int dev;
     void* fn;
@@ -273,7 +287,8 @@ int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, int 
   Geometry best{0, 0, 0};
   for (int ci = 0; ci < ncand; ++ci) {
     const int wpc = cand[ci];
-    const size_t smem = decode_smem(wpc, depth, stage, nt, core_bytes);
+    if (pair && (wpc & 1)) continue;  // warps come in pairs
+    const size_t smem = decode_smem(wpc, depth, stage, pair, core_bytes);
     if (smem > 232448) continue;
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops.fn, wpc * 32, smem);
@@ -298,6 +313,13 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   const int D = a->head_size, bs = a->block_size;
   pl->G = a->num_q_heads / a->num_kv_heads;
   pl->nt = pl->G <= 8 ? 1 : (pl->G <= 16 ? 2 : 4);
+  // Groups of 17-32 query heads that one warp cannot hold (D = 128): two
+  // warps share each ring, 16 heads each.  At D = 64 one warp holds all 32
+  // and is faster (mqa_small_page: 54.4 against 64.9 us per call for the
+  // pair), so pairs are used there only when PAB200_PAIR=1 asks for them.
+  const bool pair_ok = pl->G > 16 && pl->G <= 32 && (D == 64 || D == 128);
+  pl->pair = pair_ok && env_int("PAB200_PAIR", pl->G * D > 2048 ? 1 : 0) != 0;
+  if (pl->pair) pl->nt = 2;
   // Tokens per ring stage: a power of two >= block_size.
   pl->st = env_int("PAB200_ST", bs <= 32 ? 32 : 64);
   if ((pl->st != 16 && pl->st != 32 && pl->st != 64) || pl->st < bs)
@@ -309,7 +331,7 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   // (PAB200_CORE=1) exists for query groups of at most 4 heads, 32-token
   // stages and D <= 128.
   pl->core = env_int("PAB200_CORE", 0) != 0 && pl->G <= pab::kCoreMaxG && pl->st == 32 && D <= 128;
-  if (!select_kernel(a->dtype, D, pl->nt, pl->st, pl->core, &pl->ops))
+  if (!select_kernel(a->dtype, D, pl->nt, pl->st, pl->core, pl->pair, &pl->ops))
     return fail(PAB200_ERR_UNSUPPORTED, "no kernel for head_size %d, group %d", D, pl->G);
 
   // Each warp owns a private ring of `depth` stages.  Throughput grows with
@@ -321,7 +343,7 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   if (depth < 2 || depth > pab::kMaxDepth)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_DEPTH must be in [2, %d]", pab::kMaxDepth);
   Geometry geo;
-  if ((rc = choose_geometry(pl->ops, dev, depth, stage, pl->nt, pab::core_q_bytes(pl->core, D),
+  if ((rc = choose_geometry(pl->ops, dev, depth, stage, pl->pair, pab::core_q_bytes(pl->core, D),
                             env_int("PAB200_WPC", 0), &geo)))
     return rc;
   const int wpc = geo.wpc, per_sm = geo.per_sm;
@@ -329,14 +351,15 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   pl->wpc = wpc;
   pl->smem = geo.smem;
   pl->ctas_per_sm = per_sm;
-  int W = sms * per_sm * wpc;
+  const int upc = pl->pair ? wpc / 2 : wpc;  // rings (work units) per CTA
+  int W = sms * per_sm * upc;
   pl->n_heads = a->num_seqs * a->num_kv_heads;
   if (a->num_splits > 1) {
     const int64_t cap = int64_t(pl->n_heads) * a->num_splits;
     if (cap < W) W = static_cast<int>(cap);
   }
   pl->W = W;
-  pl->grid = (W + wpc - 1) / wpc;
+  pl->grid = (W + upc - 1) / upc;
   // Partial-state slot: acc [G][D], m [G], l [G].
   pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
   // Workspace: status, weff and the dynamic-tail header in the first 256

@@ -52,6 +52,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar,
       : "memory");
 }
 
+// Plain arrival (release at CTA scope): completes a phase of a barrier
+// initialised with count 1 that expects no bytes.
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Barrier ID (1..15) over `threads` threads of the CTA (a multiple of 32).
+template <int ID>
+__device__ __forceinline__ void named_barrier_sync(int threads) {
+  static_assert(ID >= 1 && ID <= 15, "barrier 0 is __syncthreads");
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -82,7 +82,7 @@ def _valid_args():
     ("head_size", 96, _lib.ERR_UNSUPPORTED),
     ("block_size", 12, _lib.ERR_UNSUPPORTED),
     ("num_q_heads", 7, _lib.ERR_INVALID_ARGUMENT),     # not a multiple of Hkv
-    ("num_q_heads", 2 * 32, _lib.ERR_UNSUPPORTED),     # G*D > 2048
+    ("num_q_heads", 2 * 64, _lib.ERR_UNSUPPORTED),     # G = 64: above a warp pair's tile
     ("num_seqs", 0, _lib.ERR_INVALID_ARGUMENT),
     ("layout", 5, _lib.ERR_INVALID_ARGUMENT),
     ("q", 4098, _lib.ERR_ALIGNMENT),

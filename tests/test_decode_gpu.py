@@ -40,6 +40,10 @@ CASES = [
     (2, 2, 3, 64, 64, torch.bfloat16),
     (2, 2, 8, 256, 16, torch.bfloat16),
     (2, 2, 2, 256, 64, torch.float16),
+    # groups of 17-32 query heads (a pair of warps per ring at D = 128)
+    (2, 2, 24, 64, 16, torch.bfloat16),
+    (2, 1, 32, 128, 16, torch.bfloat16),
+    (2, 2, 20, 128, 32, torch.float16),
 ]
 
 
@@ -198,3 +202,23 @@ def test_one_long_sequence_over_every_warp(cuda_device):
     assert_close(out, run_oracle(q, k, v, sl, bt, scale), what="one 200k-token head")
     again = _b200()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), bt.to(dev), scale)
     assert torch.equal(out, again)
+
+
+@pytest.mark.parametrize("G,D", [(32, 64), (24, 64), (32, 128)])
+def test_paired_warps_match_single_warp(cuda_device, monkeypatch, G, D):
+    """A pair of warps sharing one ring (16 query heads each) gives the
+    single-warp kernel's output bit for bit: every query head's softmax and
+    accumulation are the same arithmetic in the same order.  num_splits pins
+    the work split to the same number of page ranges for both kernels."""
+    lens = [[5000, 37, 0, 1200], [1, 2600, 700, 16]]
+    q, k, v, sl, bt, scale = random_case(2, 4, G, D, 16, lens, torch.float16, seed=G + D,
+                                         k_scale=4.0)
+    dev = cuda_device
+    args = [t.to(dev) for t in (q, k, v, sl, bt)]
+    monkeypatch.setenv("PAB200_PAIR", "1")  # pairs also where one warp would do
+    paired = _b200()(*args, scale, num_splits=6)
+    assert_close(paired, run_oracle(q, k, v, sl, bt, scale), what=f"paired G{G} D{D}")
+    if G * D <= 2048:  # the single-warp kernel holds the whole group
+        monkeypatch.setenv("PAB200_PAIR", "0")
+        single = _b200()(*args, scale, num_splits=6)
+        assert torch.equal(paired, single)

@@ -157,6 +157,26 @@ def test_states_merge_both_arithmetic_paths(cuda_device, monkeypatch, core):
     assert_close(merge_packed_states(states, B, Hkv * G, D), ref, what=f"core={core}")
 
 
+@pytest.mark.parametrize("G,D", [(32, 64), (24, 128)])
+def test_paired_warps_states_merge(cuda_device, monkeypatch, G, D):
+    """Partial states of a group split over a pair of warps (each warp writes
+    its 16 query heads' rows) merge to the oracle's output."""
+    monkeypatch.setenv("PAB200_PAIR", "1")
+    B, Hkv, bs = 2, 2, 16
+    q, pk, pv, bt, lens, scale = _pool_case(B, Hkv, G, D, bs, [900, 130], torch.bfloat16,
+                                            seed=G)
+    ref = run_oracle(*_reference_view(q, pk, pv, bt, lens), scale)[:, 0]
+    dev = cuda_device
+    starts, ends = context_ranges(lens, 3, 64)
+    S = state_numel(B, Hkv * G, D)
+    states = torch.empty((3, S), dtype=torch.float32, device=dev)
+    for r in range(3):
+        btl, ll = local_view(bt, lens, starts[r], ends[r], bs)
+        paged_attention_states(q.to(dev), pk.to(dev), pv.to(dev), btl.to(dev), ll.to(dev), scale,
+                               bs, state=states[r])
+    assert_close(merge_packed_states(states, B, Hkv * G, D), ref, what=f"paired G{G} D{D}")
+
+
 @pytest.mark.parametrize("state_mode", [False, True])
 def test_back_to_back_calls_reuse_outputs(cuda_device, state_mode):
     """Calls queued back to back on one stream into the same output: the
