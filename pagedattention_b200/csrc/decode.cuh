@@ -122,6 +122,7 @@ struct DecodeParams {
   int32_t* empty;              // [n_heads] their indices (zeroed by the decode grid)
   int32_t steal_m_max;         // tail chunks per warp the workspace holds
   int32_t steal_pps;           // pages per ring stage (ST / block_size)
+  int32_t steal_min_stages;    // smallest tail chunk, in ring stages
   // [(n_heads + W * (steal_m_max + 1)) * slot_floats] partial states, one
   // per (head, segment) pair; slot layout: acc [G][D], m [G], l [G]
   float* part;
@@ -340,15 +341,20 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   // include them; capping W at the page count gives every warp >= 1 page.
   const int W = static_cast<int>(total < p.total_warps ? total : p.total_warps);
   // Dynamic tail: about a quarter of every range, in at most steal_m_max
-  // chunks of whole stages; none when ranges are shorter than four stages.
+  // chunks of whole stages, each at least steal_min_stages long; none when
+  // the tail is shorter than that.  (A claim costs a few dependent L2
+  // atomics, as long as streaming a stage or two: short chunks cost more
+  // than the balance they buy.)
   int sm_m = 0, sm_k = 0;
   if (W > 1 && p.steal_m_max > 0) {
     const int ppw = static_cast<int>(total / W);
     const int tail = ppw / 4;
     const int pps = p.steal_pps;
-    if (tail >= pps) {
+    const int kmin = pps * (p.steal_min_stages > 1 ? p.steal_min_stages : 1);
+    if (tail >= kmin) {
       const int each = (tail + p.steal_m_max - 1) / p.steal_m_max;
       sm_k = (each + pps - 1) / pps * pps;
+      if (sm_k < kmin) sm_k = kmin;
       sm_m = tail / sm_k;
       if (sm_m > p.steal_m_max) sm_m = p.steal_m_max;
       if (sm_m == 0) sm_k = 0;

@@ -569,6 +569,7 @@ int decode_impl(const pab200_decode_args* a, const pab::AppendParams* app, void*
   p.empty = reinterpret_cast<int32_t*>(ws + pl.off_empty);
   p.steal_m_max = pl.steal_m_max;
   p.steal_pps = pl.st / a->block_size;
+  p.steal_min_stages = env_int("PAB200_STEAL_MIN_STAGES", 4);
   p.cum = reinterpret_cast<int32_t*>(ws + pl.off_cum);
   p.wstart = reinterpret_cast<int32_t*>(ws + pl.off_wstart);
   p.part = reinterpret_cast<float*>(ws + pl.off_part);

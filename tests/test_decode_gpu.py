@@ -105,6 +105,7 @@ def test_tail_chunks_agree(cuda_device, monkeypatch, steal_m, B, Hkv, G, D, bs, 
     run-time-claimed chunks per warp range, the merged result is the
     oracle's."""
     monkeypatch.setenv("PAB200_STEAL_M", steal_m)
+    monkeypatch.setenv("PAB200_STEAL_MIN_STAGES", "1")
     lens = [[3000 - 700 * h - 300 * s for h in range(Hkv)] for s in range(B)]
     q, k, v, sl, bt, scale = random_case(B, Hkv, G, D, bs, lens, dtype, seed=31)
     dev = cuda_device
@@ -112,10 +113,11 @@ def test_tail_chunks_agree(cuda_device, monkeypatch, steal_m, B, Hkv, G, D, bs, 
     assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"tail chunks {steal_m}")
 
 
-def test_schedule_independent_results(cuda_device):
+def test_schedule_independent_results(cuda_device, monkeypatch):
     """Which warp computes a tail chunk is decided at run time, but segments
     and merge order are fixed: many repeated calls on a batch large enough
     for every warp to own tail chunks are bit-identical."""
+    monkeypatch.setenv("PAB200_STEAL_MIN_STAGES", "1")  # one-stage chunks: many per range
     lens = [[4096 + 512 * ((s * 3 + h) % 5) for h in range(4)] for s in range(24)]
     q, k, v, sl, bt, scale = random_case(24, 4, 4, 128, 16, lens, torch.bfloat16, seed=77)
     dev = cuda_device
@@ -191,10 +193,11 @@ def test_many_short_sequences(cuda_device):
     assert_close(out, run_oracle(q, k, v, sl, bt, scale), what="2048 short sequences")
 
 
-def test_one_long_sequence_over_every_warp(cuda_device):
+def test_one_long_sequence_over_every_warp(cuda_device, monkeypatch):
     """One sequence, one kv head, 200k tokens: a single head cut into a
     static prefix and tail chunks on every warp, merged from ~1000 partial
     states (the CTA-per-row reduce)."""
+    monkeypatch.setenv("PAB200_STEAL_MIN_STAGES", "1")  # 14-page ranges keep a tail
     q, k, v, sl, bt, scale = random_case(1, 1, 8, 128, 16, [[200_000]], torch.bfloat16, seed=23,
                                          poison=False)
     dev = cuda_device
