@@ -19,9 +19,17 @@
  *  - Every pointer in pab200_decode_args is a DEVICE pointer on the current
  *    CUDA device.  Strides are in ELEMENTS, not bytes.
  *  - Calls are asynchronous on `stream`; the library never synchronises the
- *    device, never allocates device memory and keeps no per-call state
- *    outside the caller's workspace.  Two calls that overlap in time on the
- *    GPU must not share a workspace.
+ *    device.  It allocates device memory only in the exchange-buffer set-up
+ *    calls (pab200_exchange_buffer_create/open) and keeps no per-call state
+ *    outside the caller's workspace, with one exception:
+ *    pab200_decode_noalloc() runs on a fixed scratch array that is part of
+ *    the library image (one per device) and whose contents persist from one
+ *    call to the next.
+ *  - Consecutive calls on one stream may share a workspace whatever their
+ *    shapes: a call whose workspace layout differs from the previous call's
+ *    waits for that call to finish before writing to it.  Two calls that can
+ *    overlap in time on the GPU (different streams with no ordering between
+ *    them) must not share a workspace.
  *  - Return value: PAB200_OK (0) or a negative pab200_status code; the text of
  *    the last error on the calling thread is available from
  *    pab200_last_error().
@@ -137,7 +145,10 @@ typedef struct pab200_decode_args {
 
 /* Bytes of workspace pab200_decode() needs for these arguments on the
  * current device (0 if the arguments are invalid; see pab200_last_error()).
- * Replaces the partial-buffer allocations of src/kernel_triton.py:232-243. */
+ * Replaces the partial-buffer allocations of src/kernel_triton.py:232-243.
+ * It grows with num_seqs * num_kv_heads and with the query group: a few MB
+ * for the batches of the benchmark workloads, ~30 MB for 256 sequences x 8
+ * kv heads x 8 query heads at head_size 128. */
 size_t pab200_decode_workspace_size(const pab200_decode_args* args);
 
 /* Number of kernel launches pab200_decode() makes for these arguments on the
@@ -175,16 +186,23 @@ int pab200_decode(const pab200_decode_args* args, void* workspace,
  * It calls no allocating routine.
  *
  * Limits and rules:
- *  - Calls whose workspace (pab200_decode_workspace_size()) exceeds
- *    PAB200_NOALLOC_SCRATCH_BYTES fail with PAB200_ERR_WORKSPACE; use
- *    pab200_decode() with a caller workspace for those.
+ *  - The plan is fitted to the scratch: where pab200_decode_workspace_size()
+ *    exceeds PAB200_NOALLOC_SCRATCH_BYTES, the call first uses fewer
+ *    run-time tail chunks per warp (results then agree with pab200_decode()
+ *    to rounding, not bit for bit, because split heads merge their partial
+ *    states in another grouping); calls that do not fit even without tail
+ *    chunks fail with PAB200_ERR_WORKSPACE.  Use pab200_decode() with a
+ *    caller workspace for those.
  *  - The first call on a device, made with that device current, looks up the
  *    scratch array's device address; make that first call before any stream
  *    capture begins.
  *  - All calls on a device share the one scratch array and it keeps the last
  *    call's contents (the planner kernel of every call re-initialises the
- *    parts that must start at zero), so calls that can overlap on the GPU
- *    (different streams without ordering between them) race: serialise them.
+ *    parts that must start at zero).  Calls queued on ONE stream are ordered
+ *    correctly whatever their shapes (a call whose scratch layout differs
+ *    from the previous call's waits for it before writing).  Calls that can
+ *    overlap on the GPU (different streams without ordering between them,
+ *    or several host threads on different streams) race: serialise them.
  *  - pab200_read_status() does not see this scratch; device status bits of
  *    these calls are not reported. */
 int pab200_decode_noalloc(const pab200_decode_args* args, void* stream);
@@ -195,7 +213,9 @@ int pab200_decode_noalloc(const pab200_decode_args* args, void* stream);
  * contiguous, caches [num_pages, block_size, head_size] contiguous,
  * block_tables [num_seqs, num_kv_heads, max_blocks] contiguous int32,
  * context_lens [num_seqs, num_kv_heads] contiguous int32.  Same semantics
- * and workspace rules as pab200_decode(). */
+ * and workspace rules as pab200_decode(); num_splits is 0 (the device-sized
+ * split).  pab200_paged_attention_workspace_size() gives the workspace it
+ * needs. */
 int pab200_paged_attention(void* out, const void* query, const void* key_cache,
                            const void* value_cache, const int32_t* block_tables,
                            const int32_t* context_lens, float scale,
@@ -204,6 +224,16 @@ int pab200_paged_attention(void* out, const void* query, const void* key_cache,
                            int32_t head_size, int32_t max_blocks,
                            int64_t num_pages, void* workspace,
                            size_t workspace_bytes, void* stream);
+
+/* Workspace bytes pab200_paged_attention() needs for these sizes on the
+ * current device (0 if they are invalid; see pab200_last_error()), without
+ * the pointers: what the flat binding of the reference's decode wrapper
+ * (src/kernel_triton.py:181-307, whose partial buffers it replaces,
+ * :232-243) sizes its cached workspace with. */
+size_t pab200_paged_attention_workspace_size(int32_t dtype, int32_t num_seqs,
+                                             int32_t num_q_heads, int32_t num_kv_heads,
+                                             int32_t head_size, int32_t block_size,
+                                             int32_t max_blocks, int64_t num_pages);
 
 /* Merge num_states partial attention states (o, lse) into `out`, the
  * log-sum-exp combination of src/kernel_triton.py:120-174 applied across

@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "pab200_decode",
     "pab200_decode_noalloc",
     "pab200_paged_attention",
+    "pab200_paged_attention_workspace_size",
     "pab200_merge_states",
     "pab200_kv_append",
     "pab200_decode_append",
@@ -168,6 +169,10 @@ def load() -> ctypes.CDLL:
         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
         ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.pab200_paged_attention.restype = ctypes.c_int
+    lib.pab200_paged_attention_workspace_size.argtypes = [
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_int64]
+    lib.pab200_paged_attention_workspace_size.restype = ctypes.c_size_t
     lib.pab200_kv_append.argtypes = [ctypes.POINTER(KvAppendArgs), ctypes.c_void_p]
     lib.pab200_kv_append.restype = ctypes.c_int
     lib.pab200_decode_append.argtypes = [ctypes.POINTER(DecodeArgs), ctypes.POINTER(KvAppendArgs),

@@ -65,6 +65,10 @@ constexpr uint32_t kStatusNegative = 0x4u;
 constexpr uint32_t kStatusTimeout = 0x8u;
 constexpr int kMetaBytesPerSlot = 32;  // two int4 per ring slot
 constexpr int kCoreMaxG = 4;           // largest query group of the CUDA-core path
+// Early start of the decode grid: calls with at most this many (sequence,
+// kv head) pairs keep their page-count prefix in shared memory.
+constexpr int kEarlyMaxHeads = 1024;
+constexpr int kEarlyBytes = (2 * kEarlyMaxHeads + 1 + 32) * 4;  // cum, lengths, warp sums
 
 // Per-warp shared memory of the CUDA-core path: the query group in fp32.
 __host__ __device__ constexpr int core_q_bytes(bool core, int D) {
@@ -118,11 +122,22 @@ struct DecodeParams {
   // reads its own, so the two may overlap.
   int4* hseg;
   uint32_t* parity;            // which half of hseg the current call uses
+  // Layout key of the workspace: everything the region offsets below depend
+  // on (workspace address, heads, warps, tail chunks, slot size).  `key`
+  // points at the copy the last planner on this workspace stored (two int4
+  // in the fixed header); key0/key1 are this call's.
+  int4* key;
+  int4 key0, key1;
   int32_t* n_empty;            // [1] heads of length 0 in this call
   int32_t* empty;              // [n_heads] their indices (zeroed by the decode grid)
   int32_t steal_m_max;         // tail chunks per warp the workspace holds
   int32_t steal_pps;           // pages per ring stage (ST / block_size)
   int32_t steal_min_stages;    // smallest tail chunk, in ring stages
+  // Early start (no append, n_heads <= kEarlyMaxHeads, single-warp rings):
+  // the decode grid plans its own ranges and issues its first copies while
+  // the planner runs; it waits for the planner only before touching shared
+  // state (claims, outputs, status, empty heads).
+  int32_t early;
   // [(n_heads + W * (steal_m_max + 1)) * slot_floats] partial states, one
   // per (head, segment) pair; slot layout: acc [G][D], m [G], l [G]
   float* part;
@@ -134,6 +149,30 @@ struct DecodeParams {
   int32_t append;
   AppendParams app;
 };
+
+// Dynamic tail of a call with `total` pages over W warp ranges: about a
+// quarter of every range, in at most m_max chunks of whole stages (`pps`
+// pages each), each at least `min_stages` stages long; none when the tail
+// is shorter than that.  (A claim costs a few dependent L2 atomics, as long
+// as streaming a stage or two: short chunks cost more than the balance they
+// buy.)  Sets *m (chunks per range) and *k (pages per chunk).
+__host__ __device__ __forceinline__ void tail_chunks(int64_t total, int W, int m_max, int pps,
+                                                     int min_stages, int* m, int* k) {
+  *m = 0;
+  *k = 0;
+  if (W <= 1 || m_max <= 0) return;
+  const int ppw = static_cast<int>(total / W);
+  const int tail = ppw / 4;
+  const int kmin = pps * (min_stages > 1 ? min_stages : 1);
+  if (tail < kmin) return;
+  const int each = (tail + m_max - 1) / m_max;
+  int kk = (each + pps - 1) / pps * pps;
+  if (kk < kmin) kk = kmin;
+  int mm = tail / kk;
+  if (mm > m_max) mm = m_max;
+  *m = mm;
+  *k = mm == 0 ? 0 : kk;
+}
 
 // The warp that owns global page P (0 <= P < T).  Warp w owns pages
 // [floor(w*T/W), floor((w+1)*T/W)).
@@ -264,12 +303,32 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   const int n_heads = p.B * p.Hkv;
   const int cap = p.maxb * p.bs;
   const int Hq = p.Hkv * p.G;
+  __shared__ int same_layout;
   grid_launch_dependents();  // the decode grid may start its prologue now
   // This kernel may run while the previous call's reduce kernel drains (it
   // is launched with programmatic dependent launch and that kernel triggers
-  // once it has read its parity): it writes only state that kernel no longer
-  // reads, the other half of hseg, and waits for it before completing.
+  // once it has read its parity).  When the previous call on this workspace
+  // had the same layout (same key: same region offsets), it writes only
+  // state that kernel no longer reads — the other half of hseg, cum, wstart,
+  // claims, the empty list — and waits for it before completing.  Any other
+  // layout (a different batch shape, split count or query group, a workspace
+  // reused at another size, or one never used before) could put cum, hseg or
+  // the empty list on top of the partial states that reduce still reads, so
+  // the kernel first waits for the previous grid to complete and only then
+  // writes anything.
   if (tid == 0) {
+    const volatile int* k = reinterpret_cast<const volatile int*>(p.key);
+    same_layout = k[0] == p.key0.x && k[1] == p.key0.y && k[2] == p.key0.z &&
+                  k[3] == p.key0.w && k[4] == p.key1.x && k[5] == p.key1.y &&
+                  k[6] == p.key1.z && k[7] == p.key1.w;
+  }
+  __syncthreads();
+  if (!same_layout) grid_dependency_wait();  // uniform across the CTA
+  if (tid == 0) {
+    if (!same_layout) {
+      p.key[0] = p.key0;
+      p.key[1] = p.key1;
+    }
     *p.status = 0u;
     *p.n_empty = 0;
     par_sm = (*reinterpret_cast<volatile uint32_t*>(p.parity) ^ 1u) & 1u;
@@ -340,26 +399,9 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   // count of a head (warp_of_page(last) - warp_of_page(first) + 1) would
   // include them; capping W at the page count gives every warp >= 1 page.
   const int W = static_cast<int>(total < p.total_warps ? total : p.total_warps);
-  // Dynamic tail: about a quarter of every range, in at most steal_m_max
-  // chunks of whole stages, each at least steal_min_stages long; none when
-  // the tail is shorter than that.  (A claim costs a few dependent L2
-  // atomics, as long as streaming a stage or two: short chunks cost more
-  // than the balance they buy.)
+  // Dynamic tail chunks of every warp range (tail_chunks).
   int sm_m = 0, sm_k = 0;
-  if (W > 1 && p.steal_m_max > 0) {
-    const int ppw = static_cast<int>(total / W);
-    const int tail = ppw / 4;
-    const int pps = p.steal_pps;
-    const int kmin = pps * (p.steal_min_stages > 1 ? p.steal_min_stages : 1);
-    if (tail >= kmin) {
-      const int each = (tail + p.steal_m_max - 1) / p.steal_m_max;
-      sm_k = (each + pps - 1) / pps * pps;
-      if (sm_k < kmin) sm_k = kmin;
-      sm_m = tail / sm_k;
-      if (sm_m > p.steal_m_max) sm_m = p.steal_m_max;
-      if (sm_m == 0) sm_k = 0;
-    }
-  }
+  tail_chunks(total, W, p.steal_m_max, p.steal_pps, p.steal_min_stages, &sm_m, &sm_k);
   if (tid == 0) {
     *p.weff = W;
     p.steal[0] = sm_m;
@@ -594,44 +636,101 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   const int upc = PAIR ? (wpc >> 1) : wpc;
   const int gw = blockIdx.x * upc + unit;
   const int g_lo = PAIR ? role * NT * 8 : 0;  // first query head of this warp
-  // Everything below reads what the planner wrote.  The start-up values are
-  // independent loads, issued together (wstart has total_warps entries, so
-  // the read is in bounds even for a warp that then exits).
-  grid_dependency_wait();
   const int n_heads = p.B * p.Hkv;
-  const int W = *p.weff;  // min(total_warps, total pages), set by the planner
-  // Total pages < 2^31 (checked on the host), so page indices are 32-bit.
-  const int total = p.cum[n_heads];
-  const int first_head = gw < p.total_warps ? p.wstart[gw] : 0;
-  const int4 steal = *reinterpret_cast<const int4*>(p.steal);
-  const int n_empty = *p.n_empty;
   // Heads of length 0 get zeros (an empty state in state mode), matching
   // softmax over zero keys times an empty V in src/kernel_eager.py:51-53.
-  for (int e = gw; e < n_empty; e += p.total_warps) {
-    const int hd = p.empty[e];
-    const int s = hd / p.Hkv, h = hd - s * p.Hkv;
-    const int Hq = p.Hkv * p.G;
-    const int g_hi = PAIR ? min(p.G, g_lo + NT * 8) : p.G;
-    for (int g = g_lo; g < g_hi; ++g) {
-      const int qh = h * p.G + g;
-      for (int c = lane * 4; c < D; c += 128) {
-        if (p.state_o)
-          *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + c) =
-              make_float4(0.f, 0.f, 0.f, 0.f);
-        else
-          *reinterpret_cast<uint2*>(static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + c) =
-              make_uint2(0u, 0u);
+  // The planner lists them; this runs after the wait for the planner.
+  auto zero_empty_heads = [&]() {
+    const int n_empty = *p.n_empty;
+    for (int e = gw; e < n_empty; e += p.total_warps) {
+      const int hd = p.empty[e];
+      const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+      const int Hq = p.Hkv * p.G;
+      const int g_hi = PAIR ? min(p.G, g_lo + NT * 8) : p.G;
+      for (int g = g_lo; g < g_hi; ++g) {
+        const int qh = h * p.G + g;
+        for (int c = lane * 4; c < D; c += 128) {
+          if (p.state_o)
+            *reinterpret_cast<float4*>(p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D + c) =
+                make_float4(0.f, 0.f, 0.f, 0.f);
+          else
+            *reinterpret_cast<uint2*>(static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh + c) =
+                make_uint2(0u, 0u);
+        }
+        if (p.state_o && lane == 0) p.state_lse[static_cast<int64_t>(s) * Hq + qh] = -INFINITY;
       }
-      if (p.state_o && lane == 0) p.state_lse[static_cast<int64_t>(s) * Hq + qh] = -INFINITY;
     }
+  };
+  // Early start: the page-count prefix of every head, computed by this CTA
+  // from the lengths (inputs: nothing the kernels before this one in the
+  // stream write, as the host enables it only for calls without an append)
+  // into shared memory — cum_sm [n_heads + 1], len_sm [n_heads] (clamped).
+  // The planner computes the same prefix for the reduce kernel; both clamp
+  // alike, so ranges, tail chunks and segments agree.
+  const bool early = !PAIR && p.early != 0;
+  int* const cum_sm = reinterpret_cast<int*>(
+      smem + upc * depth * STAGE_BYTES + upc * kMaxDepth * (8 + kMetaBytesPerSlot) +
+      upc * core_q_bytes(CORE, D));
+  int* const len_sm = cum_sm + kEarlyMaxHeads + 1;
+  int W, total, first_head = 0, sm_m, sm_k;
+  if (early) {
+    int* const wsum = len_sm + kEarlyMaxHeads;  // [32] per-warp sums
+    const int nt = blockDim.x;
+    const int per = (n_heads + nt - 1) / nt;
+    const int h0 = threadIdx.x * per, h1 = min(h0 + per, n_heads);
+    const int capl = p.maxb * p.bs;
+    int sum = 0;
+    for (int hd = h0; hd < h1; ++hd) {
+      const int s = hd / p.Hkv, h = hd - s * p.Hkv;
+      int L = p.lens[s * p.l_sb + h * p.l_sh];
+      L = L < 0 ? 0 : (L > capl ? capl : L);
+      len_sm[hd] = L;
+      sum += (L + p.bs - 1) / p.bs;
+    }
+    int x = sum;  // inclusive scan within the warp, then across warps
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    int run = x - sum;
+    for (int w = 0; w < warp; ++w) run += wsum[w];
+    for (int hd = h0; hd < h1; ++hd) {
+      cum_sm[hd] = run;
+      run += (len_sm[hd] + p.bs - 1) / p.bs;
+    }
+    if (threadIdx.x == nt - 1) cum_sm[n_heads] = run;
+    __syncthreads();
+    total = cum_sm[n_heads];
+    W = total < p.total_warps ? total : p.total_warps;
+    tail_chunks(total, W, p.steal_m_max, p.steal_pps, p.steal_min_stages, &sm_m, &sm_k);
+  } else {
+    // Everything below reads what the planner wrote.  The start-up values
+    // are independent loads, issued together (wstart has total_warps
+    // entries, so the read is in bounds even for a warp that then exits).
+    grid_dependency_wait();
+    W = *p.weff;  // min(total_warps, total pages), set by the planner
+    // Total pages < 2^31 (checked on the host), so page indices are 32-bit.
+    total = p.cum[n_heads];
+    first_head = gw < p.total_warps ? p.wstart[gw] : 0;
+    const int4 steal = *reinterpret_cast<const int4*>(p.steal);
+    sm_m = steal.x;
+    sm_k = steal.y;
+    zero_empty_heads();
   }
-  if (gw >= W || total == 0) return;
-  const int sm_m = steal.x, sm_k = steal.y;
+  const int gs = gw < W ? static_cast<int>(static_cast<int64_t>(gw) * total / W) : 0;
+  const int g_end = gw < W ? static_cast<int>(static_cast<int64_t>(gw + 1) * total / W) : 0;
+  if (gw >= W || total == 0 || gs >= g_end) {
+    if (early) {
+      grid_dependency_wait();
+      zero_empty_heads();
+    }
+    return;
+  }
   // The reduce grid may be scheduled now; it waits for this grid to complete.
-  grid_launch_dependents();
-  const int gs = static_cast<int>(static_cast<int64_t>(gw) * total / W);
-  const int g_end = static_cast<int>(static_cast<int64_t>(gw + 1) * total / W);
-  if (gs >= g_end) return;
+  if (!early) grid_launch_dependents();
   // Current segment [c_gp, ge): the static prefix first, then tail chunks
   // claimed from the front of this warp's tail, then chunks stolen from the
   // back of other warps' tails.  run_start is the segment's first page.
@@ -689,6 +788,11 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   auto load_window = [&](int w0) {
     win = w0;
     const int hd = w0 + lane;
+    if (early) {
+      win_cum = (hd <= n_heads) ? cum_sm[hd] : 0;
+      win_len = (hd < n_heads) ? len_sm[hd] : 0;
+      return;
+    }
     win_cum = (hd <= n_heads) ? p.cum[hd] : 0;
     int L = 0;
     if (hd < n_heads) {
@@ -719,9 +823,6 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
       c_slot = segment_of_page(c_lo > run_start ? c_lo : run_start, total, W, sm_m, sm_k);
     }
   };
-  load_window(first_head);
-  enter_head(win);
-
   // Largest head hd with cum[hd] <= P (the head holding global page P):
   // 32 probes per round narrow the range 32-fold.
   auto find_head = [&](int P) -> int {
@@ -729,13 +830,17 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     while (hi - lo > 1) {
       const int step = (hi - lo + 31) / 32;
       const int x = lo + lane * step;
-      const bool le = x < hi && p.cum[x] <= P;  // true for lane 0: cum[lo] <= P
+      // true for lane 0: cum[lo] <= P
+      const bool le = x < hi && (early ? cum_sm[x] : p.cum[x]) <= P;
       const unsigned mask = __ballot_sync(0xffffffffu, le);
       lo += (31 - __clz(mask)) * step;
       hi = lo + step < hi ? lo + step : hi;
     }
     return lo;
   };
+  if (early) first_head = find_head(gs);
+  load_window(first_head);
+  enter_head(win);
   // Claim a tail chunk of another warp (from the back of its tail).  Each
   // round reads the claim words of 32 warps picked by a shared cursor and
   // tries the one with the most chunks left; gives up once the planner's
@@ -814,12 +919,22 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     return false;
   };
 
+  // Before the wait for the planner (early start) no claim may be made and
+  // no status bit raised: the planner has not yet reset them.
+  bool prewait = early;
+  bool deferred = false;    // the static prefix ended before the wait
+  bool pending_bad = false;  // a bad page id seen before the wait
   // Next stage, prepared one issue ahead so its block-table loads overlap.
   bool nx_valid = false;
   int nx_head = 0, nx_h = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_slot = 0, nx_vfirst = 0,
       nx_vlast = 0;
   int64_t nx_pid = 0;  // lane i < nx_np: page id of page i of the stage
   auto prepare_next = [&]() {
+    if (c_gp >= ge && prewait) {
+      nx_valid = false;
+      deferred = true;
+      return;
+    }
     if (c_gp >= ge && !next_region()) {
       nx_valid = false;
       return;
@@ -835,7 +950,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     nx_np = np;
     // The segment's last stage: claim this warp's next tail chunk now, so the
     // atomic completes while the stages in flight are computed.
-    if (mode == 0 && sm_m > 0 && !claim_sent && c_gp + np >= ge) {
+    if (mode == 0 && sm_m > 0 && !claim_sent && !prewait && c_gp + np >= ge) {
       if (lane == 0) pend = atomicAdd(p.claims + gw, 1ull);
       claim_sent = true;
     }
@@ -858,7 +973,12 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     }
     __syncwarp();
     const bool bad = lane < nx_np && (nx_pid < 0 || nx_pid >= p.num_pages);
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(p.status, kStatusBadPage);
+    if (__any_sync(0xffffffffu, bad)) {
+      if (prewait)
+        pending_bad = true;
+      else if (lane == 0)
+        atomicOr(p.status, kStatusBadPage);
+    }
     // A rejected page id reads a box that lies wholly outside the tensor
     // (negative row), which the TMA unit fills with zeros.
     const int32_t row = bad ? -256 : (static_cast<int32_t>(nx_pid) << log2_bs);
@@ -1094,6 +1214,23 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
         break;
       }
       ++issued;
+    }
+  }
+  if (early) {
+    // The first stages are in flight: now wait for the planner (it reset
+    // the status word, claim words and tail counters and listed the empty
+    // heads), then finish the start-up that touches shared state.
+    grid_dependency_wait();
+    prewait = false;
+    if (pending_bad && lane == 0) atomicOr(p.status, kStatusBadPage);
+    zero_empty_heads();
+    grid_launch_dependents();
+    if (deferred) {
+      prepare_next();
+      for (int i = issued; i < depth; ++i) {
+        if (!issue(i)) break;
+        ++issued;
+      }
     }
   }
 

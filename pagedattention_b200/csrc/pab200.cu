@@ -13,6 +13,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 
@@ -165,7 +166,7 @@ struct Plan {
   size_t smem;
   int n_heads;
   int slot_floats;
-  int steal_m_max;
+  int steal_m_max, steal_min_stages;
   size_t off_cum, off_wstart, off_claims, off_hseg, off_empty, off_part, ws_bytes;
 };
 
@@ -175,7 +176,8 @@ bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }
 
-int validate(const pab200_decode_args* a) {
+// Checks shapes, sizes and (with check_pointers) pointers and alignment.
+int validate(const pab200_decode_args* a, bool check_pointers) {
   if (!a) return fail(PAB200_ERR_INVALID_ARGUMENT, "args is null");
   if (a->dtype != PAB200_DTYPE_BF16 && a->dtype != PAB200_DTYPE_F16)
     return fail(PAB200_ERR_UNSUPPORTED, "dtype %d: q/k/v must be bf16 or f16", a->dtype);
@@ -208,6 +210,8 @@ int validate(const pab200_decode_args* a) {
     return fail(PAB200_ERR_UNSUPPORTED, "num_pages*block_size too large (>= 2^31 rows)");
   if (a->num_pages == 0 && a->max_blocks > 0)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "num_pages is 0 but max_blocks > 0");
+  if (a->num_splits < 0) return fail(PAB200_ERR_INVALID_ARGUMENT, "num_splits must be >= 0");
+  if (!check_pointers) return PAB200_OK;
   if (!a->q || !a->seqlens) return fail(PAB200_ERR_INVALID_ARGUMENT, "q or seqlens is null");
   if (!a->state_o && !a->out) return fail(PAB200_ERR_INVALID_ARGUMENT, "out is null");
   if (a->state_o && !a->state_lse)
@@ -222,18 +226,18 @@ int validate(const pab200_decode_args* a) {
     return fail(PAB200_ERR_ALIGNMENT, "state_o must be 16-byte aligned");
   if (a->num_pages > 0 && (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16)))
     return fail(PAB200_ERR_ALIGNMENT, "k_cache and v_cache must be 16-byte aligned");
-  if (a->num_splits < 0) return fail(PAB200_ERR_INVALID_ARGUMENT, "num_splits must be >= 0");
   return PAB200_OK;
 }
 
 // Dynamic shared memory of one decode CTA: ring slots, then per-warp
-// mbarriers, stage records and merge scratch (see decode_kernel).
-// A paired kernel has one ring (and a second set of mbarriers) per two warps.
+// mbarriers, stage records and CUDA-core query scratch (see decode_kernel),
+// then the early-start page-count prefix (single-warp rings).  A paired
+// kernel has one ring (and a second set of mbarriers) per two warps.
 size_t decode_smem(int wpc, int depth, size_t stage, bool pair, int core_bytes) {
   const size_t units = pair ? size_t(wpc / 2) : size_t(wpc);
   return 1024 + units * depth * stage +
          units * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + core_bytes) +
-         (pair ? units * pab::kMaxDepth * 8 : 0);
+         (pair ? units * pab::kMaxDepth * 8 : size_t(pab::kEarlyBytes));
 }
 
 struct Geometry {
@@ -301,8 +305,12 @@ int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, bool
   return PAB200_OK;
 }
 
-int make_plan(const pab200_decode_args* a, Plan* pl) {
-  int rc = validate(a);
+// Plans one call.  `scratch_cap`: largest workspace the call may use; the
+// tail-chunk count per warp (m_max) is lowered until the workspace fits it
+// (SIZE_MAX for a caller workspace, which is sized to the plan instead).
+int make_plan(const pab200_decode_args* a, Plan* pl, size_t scratch_cap,
+              bool check_pointers = true) {
+  int rc = validate(a, check_pointers);
   if (rc) return rc;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -362,13 +370,12 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
   pl->grid = (W + upc - 1) / upc;
   // Partial-state slot: acc [G][D], m [G], l [G].
   pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
-  // Workspace: status, weff and the dynamic-tail header in the first 256
-  // bytes (status, weff, parity of the current call, dynamic-tail header),
-  // then cum, wstart, claim words, per-head segment ranges for two calls,
-  // the list of empty heads and the partial slots
-  // (n_heads + W * (m_max + 1): one per (head, segment) pair).  The tail
-  // chunk count per warp is capped so that the workspace stays within the
-  // 16 MiB of the no-alloc scratch.
+  // Workspace: a 256-byte header (status, weff, parity of the current call,
+  // empty-head count, dynamic-tail header, layout key), then cum, wstart,
+  // claim words, per-head segment ranges for two calls, the list of empty
+  // heads and the partial slots (n_heads + W * (m_max + 1): one per (head,
+  // segment) pair).  Under a scratch cap the tail chunk count per warp is
+  // lowered until the workspace fits.
   int m_max = env_int("PAB200_STEAL_M", 4);
   if (m_max < 0) m_max = 0;
   for (;; --m_max) {
@@ -386,9 +393,10 @@ int make_plan(const pab200_decode_args* a, Plan* pl) {
     pl->off_part = off;
     off = align256(off + (size_t(pl->n_heads) + size_t(W) * (m_max + 1)) * pl->slot_floats * 4);
     pl->ws_bytes = off;
-    if (m_max == 0 || off <= PAB200_NOALLOC_SCRATCH_BYTES) break;
+    if (m_max == 0 || off <= scratch_cap) break;
   }
   pl->steal_m_max = m_max;
+  pl->steal_min_stages = env_int("PAB200_STEAL_MIN_STAGES", 4);
   return PAB200_OK;
 }
 
@@ -465,8 +473,18 @@ cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s, bool pdl) {
 namespace {
 // Reduce launch: while heads hold few partial states, one warp per head (or
 // per (head, query head) row when G * D > 1024); when they hold many, one CTA
-// (4 warps splitting the partials) per row.  The expected count assumes
-// equal head lengths.
+// (4 warps splitting the partials) per row.  The expected count assumes every
+// head as long as its block table allows: the warps' static ranges plus the
+// tail chunks the planner would cut for that many pages (the planner's own
+// choice, on the device, depends on the actual lengths).
+double expected_spans(const Plan& pl, const pab::DecodeParams& p) {
+  const int64_t pages = int64_t(pl.n_heads) * (p.maxb > 0 ? p.maxb : 1);
+  const int W = static_cast<int>(pages < pl.W ? pages : pl.W);
+  int m = 0, k = 0;
+  pab::tail_chunks(pages, W, pl.steal_m_max, pl.st / p.bs, pl.steal_min_stages, &m, &k);
+  return double(W) * (m + 1) / pl.n_heads + 1.0;
+}
+
 template <typename T, int D, int NCT>
 cudaError_t launch_reduce_heads(const pab::DecodeParams& p, int n_heads, cudaStream_t s, bool pdl) {
   LaunchCfg lc(dim3(static_cast<unsigned>((n_heads + 3) / 4)), dim3(128), 0, s, pdl);
@@ -475,10 +493,18 @@ cudaError_t launch_reduce_heads(const pab::DecodeParams& p, int n_heads, cudaStr
 
 template <typename T, int D>
 cudaError_t launch_reduce_d(const pab::DecodeParams& p, const Plan& pl, cudaStream_t s, bool pdl) {
-  const double spans = double(pl.W) * (pl.steal_m_max + 1) / pl.n_heads + 1.0;
-  if (spans <= 24.0) {
-    int nct = 1;  // float4 output chunks per lane: G*D/128 rounded up to a power of two
-    while (nct * 128 < pl.G * D) nct *= 2;
+  int nct = 1;  // float4 output chunks per lane: G*D/128 rounded up to a power of two
+  while (nct * 128 < pl.G * D) nct *= 2;
+  // Dependent rounds of partial-state loads per row: the warp-per-head (or
+  // per-row) kernel keeps 16/nct (16) partials in flight per warp; the
+  // CTA-per-row kernel splits a row's partials over 4 warps, 16 in flight
+  // each, and spends about one more round combining them.  The fewer rounds
+  // win; ties go to the warp-per-head kernel (fewer CTAs).
+  const double spans = expected_spans(pl, p);
+  const double in_flight = nct > 8 ? 16.0 : 16.0 / nct;
+  const double rounds_heads = std::ceil(spans / in_flight);
+  const double rounds_split = std::ceil(spans / 64.0) + 1.0;
+  if (rounds_heads <= rounds_split) {
     switch (nct) {
       case 1: return launch_reduce_heads<T, D, 1>(p, pl.n_heads, s, pdl);
       case 2: return launch_reduce_heads<T, D, 2>(p, pl.n_heads, s, pdl);
@@ -508,23 +534,25 @@ cudaError_t launch_reduce(const pab::DecodeParams& p, const Plan& pl, cudaStream
 
 PAB200_EXPORT size_t pab200_decode_workspace_size(const pab200_decode_args* args) {
   Plan pl;
-  if (make_plan(args, &pl) != PAB200_OK) return 0;
+  if (make_plan(args, &pl, SIZE_MAX) != PAB200_OK) return 0;
   return pl.ws_bytes;
 }
 
 PAB200_EXPORT int pab200_decode_launch_count(const pab200_decode_args* args) {
   Plan pl;
-  if (make_plan(args, &pl) != PAB200_OK) return 0;
+  if (make_plan(args, &pl, SIZE_MAX) != PAB200_OK) return 0;
   return 3;
 }
 
 namespace {
-// One decode call; with `app`, the planner first appends the step's tokens.
-int decode_impl(const pab200_decode_args* a, const pab::AppendParams* app, void* workspace,
-                size_t workspace_bytes, void* stream) {
-  Plan pl;
-  int rc = make_plan(a, &pl);
-  if (rc) return rc;
+constexpr int kLayoutKeyMagic = 0x50414232;
+constexpr size_t kLayoutKeyOffset = 32;  // two int4 in the workspace header
+
+// One decode call planned as `pl`; with `app`, the planner first appends the
+// step's tokens.
+int decode_impl(const pab200_decode_args* a, const Plan& pl, const pab::AppendParams* app,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = PAB200_OK;
   if (!workspace || workspace_bytes < pl.ws_bytes)
     return fail(PAB200_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", pl.ws_bytes,
                 workspace ? workspace_bytes : size_t(0));
@@ -567,9 +595,16 @@ int decode_impl(const pab200_decode_args* a, const pab::AppendParams* app, void*
   p.parity = reinterpret_cast<uint32_t*>(ws + 8);
   p.n_empty = reinterpret_cast<int32_t*>(ws + 12);
   p.empty = reinterpret_cast<int32_t*>(ws + pl.off_empty);
+  // The region offsets are functions of (n_heads, W, m_max, slot_floats);
+  // with the workspace address they make the key the planner compares.
+  p.key = reinterpret_cast<int4*>(ws + kLayoutKeyOffset);
+  const uint64_t wsa = reinterpret_cast<uintptr_t>(workspace);
+  p.key0 = make_int4(static_cast<int>(wsa & 0xffffffffu), static_cast<int>(wsa >> 32),
+                     pl.n_heads, pl.W);
+  p.key1 = make_int4(pl.steal_m_max, pl.slot_floats, kLayoutKeyMagic, 0);
   p.steal_m_max = pl.steal_m_max;
   p.steal_pps = pl.st / a->block_size;
-  p.steal_min_stages = env_int("PAB200_STEAL_MIN_STAGES", 4);
+  p.steal_min_stages = pl.steal_min_stages;
   p.cum = reinterpret_cast<int32_t*>(ws + pl.off_cum);
   p.wstart = reinterpret_cast<int32_t*>(ws + pl.off_wstart);
   p.part = reinterpret_cast<float*>(ws + pl.off_part);
@@ -577,6 +612,11 @@ int decode_impl(const pab200_decode_args* a, const pab::AppendParams* app, void*
   p.state_o = a->state_o;
   p.state_lse = a->state_lse;
   p.append = app ? 1 : 0;
+  // Early start of the decode grid (see DecodeParams::early): not with an
+  // append (the planner writes the lengths and the cache the decode reads)
+  // nor with warp pairs, and only while the prefix fits shared memory.
+  p.early = !app && !pl.pair && pl.n_heads <= pab::kEarlyMaxHeads &&
+            env_int("PAB200_EARLY", 1) != 0;
   if (app) {
     p.app = *app;
     p.app.status = p.status;  // append bits land in the call's status word
@@ -618,7 +658,10 @@ int decode_impl(const pab200_decode_args* a, const pab::AppendParams* app, void*
 
 PAB200_EXPORT int pab200_decode(const pab200_decode_args* a, void* workspace,
                                 size_t workspace_bytes, void* stream) {
-  return decode_impl(a, nullptr, workspace, workspace_bytes, stream);
+  Plan pl;
+  const int rc = make_plan(a, &pl, SIZE_MAX);
+  if (rc) return rc;
+  return decode_impl(a, pl, nullptr, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------- no-alloc
@@ -652,7 +695,7 @@ int noalloc_scratch(void** out) {
 
 PAB200_EXPORT int pab200_decode_noalloc(const pab200_decode_args* a, void* stream) {
   Plan pl;
-  int rc = make_plan(a, &pl);
+  int rc = make_plan(a, &pl, PAB200_NOALLOC_SCRATCH_BYTES);
   if (rc) return rc;
   if (pl.ws_bytes > PAB200_NOALLOC_SCRATCH_BYTES)
     return fail(PAB200_ERR_WORKSPACE,
@@ -661,16 +704,18 @@ PAB200_EXPORT int pab200_decode_noalloc(const pab200_decode_args* a, void* strea
                 pl.ws_bytes, PAB200_NOALLOC_SCRATCH_BYTES);
   void* ws = nullptr;
   if ((rc = noalloc_scratch(&ws))) return rc;
-  return pab200_decode(a, ws, PAB200_NOALLOC_SCRATCH_BYTES, stream);
+  return decode_impl(a, pl, nullptr, ws, PAB200_NOALLOC_SCRATCH_BYTES, stream);
 }
 
-PAB200_EXPORT int pab200_paged_attention(void* out, const void* query, const void* key_cache,
-                                         const void* value_cache, const int32_t* block_tables,
-                                         const int32_t* context_lens, float scale,
-                                         int32_t block_size, int32_t dtype, int32_t num_seqs,
-                                         int32_t num_q_heads, int32_t num_kv_heads,
-                                         int32_t head_size, int32_t max_blocks, int64_t num_pages,
-                                         void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+// Arguments of the flat north-star entry point: the reference page layout,
+// every tensor contiguous.
+pab200_decode_args flat_args(void* out, const void* query, const void* key_cache,
+                             const void* value_cache, const int32_t* block_tables,
+                             const int32_t* context_lens, float scale, int32_t block_size,
+                             int32_t dtype, int32_t num_seqs, int32_t num_q_heads,
+                             int32_t num_kv_heads, int32_t head_size, int32_t max_blocks,
+                             int64_t num_pages) {
   pab200_decode_args a{};
   a.out = out;
   a.q = query;
@@ -700,6 +745,36 @@ PAB200_EXPORT int pab200_paged_attention(void* out, const void* query, const voi
   a.bt_page_add = 0;
   a.softmax_scale = scale;
   a.num_splits = 0;
+  return a;
+}
+}  // namespace
+
+PAB200_EXPORT size_t pab200_paged_attention_workspace_size(int32_t dtype, int32_t num_seqs,
+                                                           int32_t num_q_heads,
+                                                           int32_t num_kv_heads,
+                                                           int32_t head_size,
+                                                           int32_t block_size,
+                                                           int32_t max_blocks,
+                                                           int64_t num_pages) {
+  const pab200_decode_args a =
+      flat_args(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1.f, block_size, dtype,
+                num_seqs, num_q_heads, num_kv_heads, head_size, max_blocks, num_pages);
+  Plan pl;
+  if (make_plan(&a, &pl, SIZE_MAX, /*check_pointers=*/false) != PAB200_OK) return 0;
+  return pl.ws_bytes;
+}
+
+PAB200_EXPORT int pab200_paged_attention(void* out, const void* query, const void* key_cache,
+                                         const void* value_cache, const int32_t* block_tables,
+                                         const int32_t* context_lens, float scale,
+                                         int32_t block_size, int32_t dtype, int32_t num_seqs,
+                                         int32_t num_q_heads, int32_t num_kv_heads,
+                                         int32_t head_size, int32_t max_blocks, int64_t num_pages,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  const pab200_decode_args a =
+      flat_args(out, query, key_cache, value_cache, block_tables, context_lens, scale,
+                block_size, dtype, num_seqs, num_q_heads, num_kv_heads, head_size, max_blocks,
+                num_pages);
   return pab200_decode(&a, workspace, workspace_bytes, stream);
 }
 
@@ -943,7 +1018,9 @@ PAB200_EXPORT int pab200_decode_append(const pab200_decode_args* a, const pab200
       app->bt_page_mul != a->bt_page_mul || app->bt_page_add != a->bt_page_add)
     return fail(PAB200_ERR_INVALID_ARGUMENT,
                 "append arguments must name the decode call's caches, block table and lengths");
-  return decode_impl(a, empty ? nullptr : &p, workspace, workspace_bytes, stream);
+  Plan pl;
+  if ((rc = make_plan(a, &pl, SIZE_MAX))) return rc;
+  return decode_impl(a, pl, empty ? nullptr : &p, workspace, workspace_bytes, stream);
 }
 
 PAB200_EXPORT int pab200_read_status(const void* workspace, uint32_t* status_out, void* stream) {

@@ -1,8 +1,10 @@
 """Generate the golden decode vectors in tests/golden/*.npz from the reference.
 
-Run in a container that has the reference checkout (read-only is fine):
+Run in a container that has the reference checkout (read-only is fine),
+naming its root with --reference or the PAB200_REFERENCE environment
+variable:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 It imports the reference's own ``flash_attn_with_kvcache_wrapper_eager``
 (src/kernel_eager.py:29-56) and runs it on CPU in float32 on seeded inputs in
@@ -21,6 +23,7 @@ reference run in the 16-bit dtype itself, for information).
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -79,8 +82,11 @@ def make_case(name, spec, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PAB200_REFERENCE"),
+                    help="root of the reference checkout (default: $PAB200_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or PAB200_REFERENCE")
     sys.path.insert(0, str(Path(args.reference) / "src"))
     from kernel_eager import flash_attn_with_kvcache_wrapper_eager  # the reference
 

@@ -5,6 +5,7 @@ import pytest
 import torch
 
 from oracle import eager as oracle
+from oracle import eager_torch
 from tests.util import ATOL, RTOL, golden_names, load_golden, random_case, run_oracle
 
 
@@ -20,6 +21,31 @@ def test_oracle_matches_reference_golden(name):
         c["q"].float().numpy(), c["k_cache"].float().numpy(), c["v_cache"].float().numpy(),
         c["cache_seqlens"].numpy(), c["block_table"].numpy(), c["softmax_scale"])
     np.testing.assert_allclose(out, c["out_fp32"].numpy(), atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_torch_restatement_matches_reference_golden(name):
+    """oracle/eager_torch.py (the CPU baseline's restatement, the reference's
+    own torch operations) reproduces src/kernel_eager.py's fp32 output, and in
+    the 16-bit dtype its native output."""
+    c = load_golden(name)
+    args = (c["k_cache"], c["v_cache"], c["cache_seqlens"], c["block_table"], c["softmax_scale"])
+    out = eager_torch.flash_attn_with_kvcache(c["q"].float(), args[0].float(), args[1].float(),
+                                             *args[2:])
+    np.testing.assert_allclose(out.numpy(), c["out_fp32"].numpy(), atol=1e-5, rtol=1e-5)
+    native = eager_torch.flash_attn_with_kvcache(c["q"], *args)
+    assert native.dtype == c["q"].dtype
+    assert torch.isclose(native.float(), c["out_native"], atol=1e-2, rtol=1e-2).all()
+
+
+def test_torch_restatement_batched_equals_port():
+    """Batch > 1 (flattened as the reference's batch==1 call) agrees with the
+    numpy port on poisoned random inputs, empty heads included."""
+    q, k, v, sl, bt, scale = random_case(3, 2, 4, 64, 16, [[40, 0], [100, 17], [1, 300]],
+                                         torch.float32, seed=5)
+    out = eager_torch.flash_attn_with_kvcache(q, k, v, sl, bt, scale)
+    ref = run_oracle(q, k, v, sl, bt, scale)
+    np.testing.assert_allclose(out.numpy(), ref.numpy(), atol=1e-5, rtol=1e-5)
 
 
 @pytest.mark.parametrize("name", golden_names())
