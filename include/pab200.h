@@ -26,10 +26,13 @@
  *    the library image (one per device) and whose contents persist from one
  *    call to the next.
  *  - Consecutive calls on one stream may share a workspace whatever their
- *    shapes: a call whose workspace layout differs from the previous call's
- *    waits for that call to finish before writing to it.  Two calls that can
- *    overlap in time on the GPU (different streams with no ordering between
- *    them) must not share a workspace.
+ *    shapes.  A call's kernels may start while the previous call's kernels
+ *    on the stream are still running (programmatic dependent launch), but
+ *    until that call has finished they only read their inputs (lengths,
+ *    block table, query, cache) and their own shared memory: every write to
+ *    the workspace, the outputs or the cache comes after it.  Two calls that
+ *    can overlap in time on the GPU (different streams with no ordering
+ *    between them) must not share a workspace.
  *  - Return value: PAB200_OK (0) or a negative pab200_status code; the text of
  *    the last error on the calling thread is available from
  *    pab200_last_error().
@@ -199,8 +202,8 @@ int pab200_decode(const pab200_decode_args* args, void* workspace,
  *  - All calls on a device share the one scratch array and it keeps the last
  *    call's contents (the planner kernel of every call re-initialises the
  *    parts that must start at zero).  Calls queued on ONE stream are ordered
- *    correctly whatever their shapes (a call whose scratch layout differs
- *    from the previous call's waits for it before writing).  Calls that can
+ *    correctly whatever their shapes (a call writes to the scratch only
+ *    after the previous call on the stream has finished).  Calls that can
  *    overlap on the GPU (different streams without ordering between them,
  *    or several host threads on different streams) race: serialise them.
  *  - pab200_read_status() does not see this scratch; device status bits of

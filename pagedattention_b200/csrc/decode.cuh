@@ -10,7 +10,7 @@
 //   plan_kernel    one CTA.  Clamps every sequence length, prefix-sums the
 //                  page counts of all (sequence, kv head) pairs ("heads" below)
 //                  into `cum`, and gives every warp of the decode grid its
-//                  first head.  Heads of length 0 get their zero output here.
+//                  first head; lists the heads of length 0.
 //   decode_kernel  persistent.  The concatenation of all heads' pages is cut
 //                  into W equal contiguous ranges, one per warp (W = every
 //                  resident warp on the device), so the load is balanced to a
@@ -38,9 +38,17 @@
 //                  (the reduce kernel of the reference): one warp per head
 //                  (lanes over its G x D outputs) or per (head, query head)
 //                  row for large groups, or, when heads have many partials,
-//                  one CTA per row whose warps split the partials.  Both are
-//                  launched early (programmatic dependent launch) and wait
-//                  for the decode grid.
+//                  one CTA per row whose warps split the partials.
+//
+// Launch chain (programmatic dependent launch): every kernel lets the next
+// one start before it ends, and every kernel writes nothing before its
+// dependency wait — until then it only reads inputs and its own shared
+// memory.  So the next call's planner and decode grid start while this
+// call's decode grid drains and its reduce runs: the planner plans, the
+// decode CTAs (when the call allows an early start) prefix-sum the lengths,
+// take over SMs as this call's CTAs leave and stream their first pages; the
+// first write of a call (planner: its plan; decode: an output, a partial
+// state, a claim, a status bit) waits for the previous call to finish.
 //
 // Shared-memory stage layout (per warp, per ring slot), ST tokens:
 //   K: [D/64 planes][ST rows][128 bytes], then V with the same shape.
@@ -117,17 +125,10 @@ struct DecodeParams {
   int32_t* steal;
   unsigned long long* claims;  // [W] claim words: low 32 bits front, high back
   // [n_heads] first segment and segment count of every head (0 if empty),
-  // for two calls: .xy for parity 0, .zw for parity 1.  The planner of the
-  // next call writes the other half while the reduce of this call still
-  // reads its own, so the two may overlap.
+  // in two halves: .xy for parity 0, .zw for parity 1, used by alternate
+  // calls.
   int4* hseg;
   uint32_t* parity;            // which half of hseg the current call uses
-  // Layout key of the workspace: everything the region offsets below depend
-  // on (workspace address, heads, warps, tail chunks, slot size).  `key`
-  // points at the copy the last planner on this workspace stored (two int4
-  // in the fixed header); key0/key1 are this call's.
-  int4* key;
-  int4 key0, key1;
   int32_t* n_empty;            // [1] heads of length 0 in this call
   int32_t* empty;              // [n_heads] their indices (zeroed by the decode grid)
   int32_t steal_m_max;         // tail chunks per warp the workspace holds
@@ -302,48 +303,13 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_heads = p.B * p.Hkv;
   const int cap = p.maxb * p.bs;
-  const int Hq = p.Hkv * p.G;
-  __shared__ int same_layout;
-  grid_launch_dependents();  // the decode grid may start its prologue now
-  // This kernel may run while the previous call's reduce kernel drains (it
-  // is launched with programmatic dependent launch and that kernel triggers
-  // once it has read its parity).  When the previous call on this workspace
-  // had the same layout (same key: same region offsets), it writes only
-  // state that kernel no longer reads — the other half of hseg, cum, wstart,
-  // claims, the empty list — and waits for it before completing.  Any other
-  // layout (a different batch shape, split count or query group, a workspace
-  // reused at another size, or one never used before) could put cum, hseg or
-  // the empty list on top of the partial states that reduce still reads, so
-  // the kernel first waits for the previous grid to complete and only then
-  // writes anything.
-  if (tid == 0) {
-    const volatile int* k = reinterpret_cast<const volatile int*>(p.key);
-    same_layout = k[0] == p.key0.x && k[1] == p.key0.y && k[2] == p.key0.z &&
-                  k[3] == p.key0.w && k[4] == p.key1.x && k[5] == p.key1.y &&
-                  k[6] == p.key1.z && k[7] == p.key1.w;
-  }
-  __syncthreads();
-  if (!same_layout) grid_dependency_wait();  // uniform across the CTA
-  if (tid == 0) {
-    if (!same_layout) {
-      p.key[0] = p.key0;
-      p.key[1] = p.key1;
-    }
-    *p.status = 0u;
-    *p.n_empty = 0;
-    par_sm = (*reinterpret_cast<volatile uint32_t*>(p.parity) ^ 1u) & 1u;
-    *p.parity = par_sm;
-  }
-  if constexpr (APPEND) {
-    // The step's new tokens go into the cache first (the previous call's
-    // decode, which read the cache, has completed when this kernel runs):
-    // every row is written at the current length, then the lengths move.
-    __syncthreads();  // status reset before any append bit is raised
-    planner_append_rows(p.app, tid);
-    __syncthreads();
-    planner_append_lengths(p.app, tid);
-    __syncthreads();
-  }
+  // This kernel may start while the previous call's kernels on the stream
+  // still run (programmatic dependent launch: the previous reduce kernel
+  // lets it start at once), and it lets the decode grid start at once.  Nothing is written before the wait for the
+  // previous grid below: until then the kernel only loads the lengths
+  // (inputs) and computes the plan, so every workspace write of a call
+  // follows the end of the previous call, whatever its shapes.
+  grid_launch_dependents();
   // Thread t owns heads [t * per, (t + 1) * per): its page counts are loaded
   // in one round (up to kPer of them kept in registers), summed, and one
   // block-wide exclusive scan of the sums gives every head's first page.
@@ -364,6 +330,18 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
     }
     return (L + p.bs - 1) / p.bs;
   };
+  if constexpr (APPEND) {
+    // The step's new tokens go into the cache first, once the previous
+    // call (whose decode read the cache) has finished: every row is
+    // written at the current length, then the lengths move.
+    grid_dependency_wait();
+    if (tid == 0) *p.status = 0u;
+    __syncthreads();  // status reset before any append bit is raised
+    planner_append_rows(p.app, tid);
+    __syncthreads();
+    planner_append_lengths(p.app, tid);
+    __syncthreads();
+  }
   int pg[kPer];
   int sum = 0;
 #pragma unroll
@@ -372,6 +350,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
     sum += pg[i];
   }
   for (int hd = h0 + kPer; hd < h1; ++hd) sum += head_pages(hd);
+  // Which half of hseg this call uses: the other half from the one the
+  // last finished planner chose (any choice would do — no kernel reads hseg
+  // before this call's plan is written — but alternating keeps the halves
+  // of consecutive calls apart).
+  if (tid == 0) par_sm = (*reinterpret_cast<volatile uint32_t*>(p.parity) ^ 1u) & 1u;
   int x = sum;  // inclusive scan within the warp
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -392,9 +375,6 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   __syncthreads();
   const int64_t total = warp_tot[31];
   int run = (warp ? warp_tot[warp - 1] : 0) + x - sum;  // first page of head h0
-  if (flags) atomicOr(p.status, flags);
-  if (tid == 0) p.cum[n_heads] = static_cast<int>(total);
-
   // With more warps than pages some warps would own no page and the span
   // count of a head (warp_of_page(last) - warp_of_page(first) + 1) would
   // include them; capping W at the page count gives every warp >= 1 page.
@@ -402,19 +382,28 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   // Dynamic tail chunks of every warp range (tail_chunks).
   int sm_m = 0, sm_k = 0;
   tail_chunks(total, W, p.steal_m_max, p.steal_pps, p.steal_min_stages, &sm_m, &sm_k);
+  const uint32_t par = par_sm;
+
+  // The previous call's kernels have finished from here on: write the plan.
+  if constexpr (!APPEND) grid_dependency_wait();
   if (tid == 0) {
+    if constexpr (!APPEND) *p.status = 0u;
+    *p.n_empty = 0;
+    *p.parity = par;
     *p.weff = W;
     p.steal[0] = sm_m;
     p.steal[1] = sm_k;
     p.steal[2] = sm_m * W;  // chunks left to claim
     p.steal[3] = 0;         // thief cursor
+    p.cum[n_heads] = static_cast<int>(total);
   }
+  __syncthreads();  // status and empty count reset before the updates below
+  if (flags) atomicOr(p.status, flags);
   if (sm_m > 0)
     for (int w = tid; w < W; w += 1024) p.claims[w] = 0ull;
   // Per head: its first page, the warps whose range starts in it, its
-  // segment range, or (empty head) its zero output.
+  // segment range, or (empty head) its place in the empty list.
   const int tp = static_cast<int>(total);
-  const uint32_t par = par_sm;  // set before the scan's barriers
   auto place_head = [&](int hd, int pages) {
     const int64_t c0 = run, c1 = run + pages;
     p.cum[hd] = run;
@@ -429,8 +418,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
           make_int2(v0, segment_of_page(static_cast<int>(c1) - 1, tp, W, sm_m, sm_k) - v0 + 1);
     } else {
       // Empty head: listed here, its zero output is written by the decode
-      // grid (this kernel may overlap the previous call's reduce, which can
-      // still be writing the same output rows).
+      // grid, after its own wait for this kernel.
       reinterpret_cast<int2*>(p.hseg + hd)[par] = make_int2(0, 0);
       p.empty[atomicAdd(p.n_empty, 1)] = hd;
     }
@@ -439,10 +427,6 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
   for (int i = 0; i < kPer; ++i)
     if (h0 + i < h1) place_head(h0 + i, pg[i]);
   for (int hd = h0 + kPer; hd < h1; ++hd) place_head(hd, head_pages(hd));
-  // Complete only after the kernel before this one (the previous call's
-  // reduce): the decode grid that waits for this kernel then cannot
-  // overwrite partial states that reduce still reads.
-  if (tid == 0) grid_dependency_wait();
 }
 
 // --------------------------------------------------------------------------
@@ -637,6 +621,9 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   const int gw = blockIdx.x * upc + unit;
   const int g_lo = PAIR ? role * NT * 8 : 0;  // first query head of this warp
   const int n_heads = p.B * p.Hkv;
+  // The reduce grid may be scheduled at once: it waits for this grid to
+  // complete before it reads anything.
+  grid_launch_dependents();
   // Heads of length 0 get zeros (an empty state in state mode), matching
   // softmax over zero keys times an empty V in src/kernel_eager.py:51-53.
   // The planner lists them; this runs after the wait for the planner.
@@ -729,8 +716,6 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     }
     return;
   }
-  // The reduce grid may be scheduled now; it waits for this grid to complete.
-  if (!early) grid_launch_dependents();
   // Current segment [c_gp, ge): the static prefix first, then tail chunks
   // claimed from the front of this warp's tail, then chunks stolen from the
   // back of other warps' tails.  run_start is the segment's first page.
@@ -919,25 +904,33 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     return false;
   };
 
-  // Before the wait for the planner (early start) no claim may be made and
-  // no status bit raised: the planner has not yet reset them.
+  // Early start: the warp streams and computes without waiting for the
+  // planner (and, through it, for the previous call's reduce kernel) until
+  // its first action on shared state — an output or partial-state write, a
+  // tail-chunk claim, a status bit — and waits for it only then.  Until
+  // then a bad page id is remembered, not yet reported: the planner resets
+  // the status word.
   bool prewait = early;
-  bool deferred = false;    // the static prefix ended before the wait
-  bool pending_bad = false;  // a bad page id seen before the wait
+  bool pending_bad = false;
+  auto ensure_waited = [&]() {
+    if (!prewait) return;
+    grid_dependency_wait();
+    prewait = false;
+    if (pending_bad && lane == 0) atomicOr(p.status, kStatusBadPage);
+    zero_empty_heads();
+  };
   // Next stage, prepared one issue ahead so its block-table loads overlap.
   bool nx_valid = false;
   int nx_head = 0, nx_h = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_slot = 0, nx_vfirst = 0,
       nx_vlast = 0;
   int64_t nx_pid = 0;  // lane i < nx_np: page id of page i of the stage
   auto prepare_next = [&]() {
-    if (c_gp >= ge && prewait) {
-      nx_valid = false;
-      deferred = true;
-      return;
-    }
-    if (c_gp >= ge && !next_region()) {
-      nx_valid = false;
-      return;
+    if (c_gp >= ge) {
+      ensure_waited();  // claims and stealing touch shared state
+      if (!next_region()) {
+        nx_valid = false;
+        return;
+      }
     }
     while (c_gp >= c_hi) enter_head(c_head + 1);
     nx_valid = true;
@@ -950,7 +943,8 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     nx_np = np;
     // The segment's last stage: claim this warp's next tail chunk now, so the
     // atomic completes while the stages in flight are computed.
-    if (mode == 0 && sm_m > 0 && !claim_sent && !prewait && c_gp + np >= ge) {
+    if (mode == 0 && sm_m > 0 && !claim_sent && c_gp + np >= ge) {
+      ensure_waited();
       if (lane == 0) pend = atomicAdd(p.claims + gw, 1ull);
       claim_sent = true;
     }
@@ -1072,6 +1066,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   // segment's part becomes the partial state in slot hd + `slot` (plain
   // stores: a reduce kernel merges the head's slots after this grid).
   auto finish_head = [&](int hd, int slot, int vfirst, int vlast) {
+    ensure_waited();  // outputs and partial slots of the previous call
     const bool whole = vfirst == vlast;
     if constexpr (CORE) {
       const int s = hd / Hkv, h = hd - s * Hkv;
@@ -1216,23 +1211,6 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
       ++issued;
     }
   }
-  if (early) {
-    // The first stages are in flight: now wait for the planner (it reset
-    // the status word, claim words and tail counters and listed the empty
-    // heads), then finish the start-up that touches shared state.
-    grid_dependency_wait();
-    prewait = false;
-    if (pending_bad && lane == 0) atomicOr(p.status, kStatusBadPage);
-    zero_empty_heads();
-    grid_launch_dependents();
-    if (deferred) {
-      prepare_next();
-      for (int i = issued; i < depth; ++i) {
-        if (!issue(i)) break;
-        ++issued;
-      }
-    }
-  }
 
   // Accumulation in progress: head, segment, the head's segment range.
   int cur_head = -1, cur_slot = -1, cur_vfirst = 0, cur_vlast = 0;
@@ -1242,6 +1220,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     const int slot = it % depth;
     const uint32_t par = static_cast<uint32_t>((it / depth) & 1);
     if (role != 0 && !mbar_wait(bars + slot * 8, par, kWaitLimitNs)) {
+      ensure_waited();
       if (lane == 0) atomicOr(p.status, kStatusTimeout);
       return;  // the leader's copies are the leader's to wait for
     }
@@ -1258,6 +1237,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
       start_head(cur_head, new_head);
     }
     if (role == 0 && !mbar_wait(bars + slot * 8, par, kWaitLimitNs)) {
+      ensure_waited();
       if (lane == 0) atomicOr(p.status, kStatusTimeout);
       for (int j = it + 1; j < issued; ++j)
         mbar_wait(bars + (j % depth) * 8, static_cast<uint32_t>((j / depth) & 1),
@@ -1482,6 +1462,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
       if (sent_end) continue;
       // Refill only once the follower has released the slot (stage it).
       if (!mbar_wait(empties + slot * 8, par, kWaitLimitNs)) {
+        ensure_waited();
         if (lane == 0) atomicOr(p.status, kStatusTimeout);
         for (int j = it + 1; j < issued; ++j)
           mbar_wait(bars + (j % depth) * 8, static_cast<uint32_t>((j / depth) & 1),
@@ -1497,18 +1478,18 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     }
   }
   if (cur_head >= 0) finish_head(cur_head, cur_slot, cur_vfirst, cur_vlast);
+  ensure_waited();
 }
 
 
-// Prologue of every reduce kernel: waits for the decode grid, reads the
-// current call's parity in every thread, and only then lets the next call's
-// planner start (it flips the parity and writes the other half of hseg).
+// Prologue of every reduce kernel: lets the next call's planner start (it
+// writes nothing, the parity included, before this grid has finished),
+// waits for the decode grid's partial states, then reads the current call's
+// parity.
 __device__ __forceinline__ uint32_t reduce_prologue(const DecodeParams& p) {
-  grid_dependency_wait();  // partials written by the decode grid
-  const uint32_t par = *reinterpret_cast<volatile uint32_t*>(p.parity) & 1u;
-  __syncthreads();
   grid_launch_dependents();
-  return par;
+  grid_dependency_wait();  // partials written by the decode grid
+  return *reinterpret_cast<volatile uint32_t*>(p.parity) & 1u;
 }
 
 // Segment range of head hd for the call with parity par.

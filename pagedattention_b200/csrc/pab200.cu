@@ -371,7 +371,7 @@ int make_plan(const pab200_decode_args* a, Plan* pl, size_t scratch_cap,
   // Partial-state slot: acc [G][D], m [G], l [G].
   pl->slot_floats = (pl->G * D + 2 * pl->G + 3) & ~3;
   // Workspace: a 256-byte header (status, weff, parity of the current call,
-  // empty-head count, dynamic-tail header, layout key), then cum, wstart,
+  // empty-head count, dynamic-tail header), then cum, wstart,
   // claim words, per-head segment ranges for two calls, the list of empty
   // heads and the partial slots (n_heads + W * (m_max + 1): one per (head,
   // segment) pair).  Under a scratch cap the tail chunk count per warp is
@@ -456,10 +456,10 @@ int encode_cache_map_uncached(const pab200_decode_args* a, const void* base, CUt
   return PAB200_OK;
 }
 
-// The planner is launched with programmatic dependent launch: after the
-// previous call on this stream (whose reduce kernel lets it start once that
-// kernel has read its parity) it overlaps that reduce, and it waits for it
-// before completing.
+// The planner is launched with programmatic dependent launch: it may start
+// while the previous call's kernels on this stream still run (the previous
+// reduce kernel lets it start once every reduce CTA has read its parity),
+// loads and plans, and writes the workspace only after they have finished.
 template <typename T>
 cudaError_t launch_plan(const pab::DecodeParams& p, cudaStream_t s, bool pdl) {
   LaunchCfg lc(dim3(1), dim3(1024), 0, s, pdl);
@@ -545,9 +545,6 @@ PAB200_EXPORT int pab200_decode_launch_count(const pab200_decode_args* args) {
 }
 
 namespace {
-constexpr int kLayoutKeyMagic = 0x50414232;
-constexpr size_t kLayoutKeyOffset = 32;  // two int4 in the workspace header
-
 // One decode call planned as `pl`; with `app`, the planner first appends the
 // step's tokens.
 int decode_impl(const pab200_decode_args* a, const Plan& pl, const pab::AppendParams* app,
@@ -595,13 +592,6 @@ int decode_impl(const pab200_decode_args* a, const Plan& pl, const pab::AppendPa
   p.parity = reinterpret_cast<uint32_t*>(ws + 8);
   p.n_empty = reinterpret_cast<int32_t*>(ws + 12);
   p.empty = reinterpret_cast<int32_t*>(ws + pl.off_empty);
-  // The region offsets are functions of (n_heads, W, m_max, slot_floats);
-  // with the workspace address they make the key the planner compares.
-  p.key = reinterpret_cast<int4*>(ws + kLayoutKeyOffset);
-  const uint64_t wsa = reinterpret_cast<uintptr_t>(workspace);
-  p.key0 = make_int4(static_cast<int>(wsa & 0xffffffffu), static_cast<int>(wsa >> 32),
-                     pl.n_heads, pl.W);
-  p.key1 = make_int4(pl.steal_m_max, pl.slot_floats, kLayoutKeyMagic, 0);
   p.steal_m_max = pl.steal_m_max;
   p.steal_pps = pl.st / a->block_size;
   p.steal_min_stages = pl.steal_min_stages;
