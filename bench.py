@@ -279,6 +279,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     from pagedattention_b200 import flash_attn_with_kvcache_wrapper_b200 as decode
+    from pagedattention_b200 import paged_attention
     from pagedattention_b200.distributed import (PeerExchange, context_ranges,
                                                  decode_context_parallel, lens_of_units,
                                                  shard_heads, shard_sequences)
@@ -459,8 +460,11 @@ def run_b200(args):
     # e2e: every step copies its inputs from pinned host memory and reads its
     # output back, as a serving loop does: each step's inputs are staged on a
     # copy stream (two device buffers, so a copy overlaps the previous
-    # step's decode), and each output returns on a third stream.  The KV cache stays resident.
-    # (split mode: the per-rank block table and lengths of its token range)
+    # step's decode), the step decodes into one of two preallocated outputs
+    # through the in-place public call (paged_attention, or the context
+    # split's decode_context_parallel with out=), and each output returns on
+    # a third stream.  The KV cache stays resident.  (split mode: the
+    # per-rank block table and lengths of its token range)
     if mode == "split":
         ins = [q, seq_lens, seq_bt]
     else:
@@ -483,8 +487,9 @@ def run_b200(args):
     for h, t in zip(hosts, ins):
         h.copy_(t.cpu())
     devs = [views(b) for b in dev_packs]
-    out_shape = q[:, 0].shape if mode == "split" else q.shape
+    out_shape = q[:, 0].shape
     out_h = [torch.empty(out_shape, dtype=q.dtype).pin_memory() for _ in range(2)]
+    out_d = [torch.empty(out_shape, dtype=q.dtype, device=dev) for _ in range(2)]
     compute = torch.cuda.current_stream(dev)
     h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     staged = [torch.cuda.Event() for _ in range(2)]
@@ -493,23 +498,33 @@ def run_b200(args):
         e.record(compute)
     e2e_no = [0]
 
+    def run_into(out, qx, slx, btx, seq_bt, seq_lens):
+        i = step_no[0] % copies
+        step_no[0] += 1
+        if mode == "split":
+            kp, vp = kpool_copies[i]
+            decode_context_parallel(qx[:, 0], kp, vp, seq_bt, seq_lens, inp.scale,
+                                    w.block_size, exchange=exchange, out=out)
+        else:
+            kc, vc = caches[i]
+            paged_attention(out, qx[:, 0], kc, vc, btx, slx, inp.scale, w.block_size)
+
     def e2e_step():
         b = e2e_no[0] % 2
         e2e_no[0] += 1
+        h2d_stream.wait_event(freed[b])
         with torch.cuda.stream(h2d_stream):
-            h2d_stream.wait_event(freed[b])
             dev_packs[b].copy_(host_pack, non_blocking=True)
-            staged[b].record(h2d_stream)
+        staged[b].record(h2d_stream)
         compute.wait_event(staged[b])
         if mode == "split":
-            out = run(devs[b][0], None, None, devs[b][2], devs[b][1])
+            run_into(out_d[b], devs[b][0], None, None, devs[b][2], devs[b][1])
         else:
-            out = run(devs[b][0], devs[b][1], devs[b][2], None, None)
+            run_into(out_d[b], devs[b][0], devs[b][1], devs[b][2], None, None)
         freed[b].record(compute)
-        d2h_stream.wait_stream(compute)
+        d2h_stream.wait_event(freed[b])
         with torch.cuda.stream(d2h_stream):
-            out_h[b].copy_(out, non_blocking=True)
-        out.record_stream(d2h_stream)
+            out_h[b].copy_(out_d[b], non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -581,9 +596,11 @@ def run_b200(args):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": E,
-                    "note": "public wrapper; every step copies q, cache_seqlens and block_table "
-                            "H2D from one pinned staging buffer in one copy (a copy stream, "
-                            "two device buffers) and its output D2H; KV cache resident"},
+                    "note": "public in-place call (paged_attention / decode_context_parallel) "
+                            "into two preallocated outputs; every step copies q, cache_seqlens "
+                            "and block_table H2D from one pinned staging buffer in one copy (a "
+                            "copy stream, two device buffers) and its output D2H; KV cache "
+                            "resident"},
             "clocks": sampler.summary(),
             "graph": graph_line,
             "gpu_launches": (launches + (1 if mode == "split" else 0)) * K,

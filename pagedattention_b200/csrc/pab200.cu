@@ -22,6 +22,8 @@
 
 #define PAB200_EXPORT extern "C" __attribute__((visibility("default")))
 
+extern char** environ;  // the process environment (POSIX)
+
 namespace {
 
 thread_local char g_last_error[512] = "";
@@ -67,10 +69,37 @@ int device_sm_count(int dev) {
   return sms[dev];
 }
 
+int device_sm_count_current() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  const int n = device_sm_count(dev);
+  return n > 0 ? n : 148;
+}
+
+// Tuning variables (PAB200_*), read from the environment: one pass over
+// the environment per planned call collects the (usually zero) PAB200_
+// entries, so a call does not pay a full getenv scan per variable, and a
+// variable changed between calls is seen by the next one.
+struct EnvSnapshot {
+  const char* entries[16];
+  int n = 0;
+};
+thread_local EnvSnapshot g_env;
+
+void refresh_env() {
+  g_env.n = 0;
+  for (char** e = environ; e && *e && g_env.n < 16; ++e)
+    if (std::strncmp(*e, "PAB200_", 7) == 0) g_env.entries[g_env.n++] = *e;
+}
+
 int env_int(const char* name, int fallback) {
-  const char* v = std::getenv(name);
-  if (!v || !*v) return fallback;
-  return std::atoi(v);
+  const size_t len = std::strlen(name);
+  for (int i = 0; i < g_env.n; ++i) {
+    const char* e = g_env.entries[i];
+    if (std::strncmp(e, name, len) == 0 && e[len] == '=')
+      return e[len + 1] ? std::atoi(e + len + 1) : fallback;
+  }
+  return fallback;
 }
 
 // ------------------------------------------------------------------ kernels
@@ -310,6 +339,7 @@ int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, bool
 // (SIZE_MAX for a caller workspace, which is sized to the plan instead).
 int make_plan(const pab200_decode_args* a, Plan* pl, size_t scratch_cap,
               bool check_pointers = true) {
+  refresh_env();
   int rc = validate(a, check_pointers);
   if (rc) return rc;
   int dev = 0;
@@ -495,15 +525,19 @@ template <typename T, int D>
 cudaError_t launch_reduce_d(const pab::DecodeParams& p, const Plan& pl, cudaStream_t s, bool pdl) {
   int nct = 1;  // float4 output chunks per lane: G*D/128 rounded up to a power of two
   while (nct * 128 < pl.G * D) nct *= 2;
-  // Dependent rounds of partial-state loads per row: the warp-per-head (or
-  // per-row) kernel keeps 16/nct (16) partials in flight per warp; the
-  // CTA-per-row kernel splits a row's partials over 4 warps, 16 in flight
-  // each, and spends about one more round combining them.  The fewer rounds
-  // win; ties go to the warp-per-head kernel (fewer CTAs).
+  // Dependent rounds of partial-state loads: the warp-per-head (or per-row)
+  // kernel keeps 16/nct (16) partials in flight per warp; the CTA-per-row
+  // kernel splits a row's partials over 4 warps, 16 in flight each, and
+  // spends about one more round combining them.  Either is run in waves of
+  // about 4 resident 4-warp CTAs per SM.  The fewer rounds win; ties go to
+  // the warp-per-head kernel (fewer CTAs).
   const double spans = expected_spans(pl, p);
   const double in_flight = nct > 8 ? 16.0 : 16.0 / nct;
-  const double rounds_heads = std::ceil(spans / in_flight);
-  const double rounds_split = std::ceil(spans / 64.0) + 1.0;
+  const int64_t rows = int64_t(pl.n_heads) * pl.G;
+  const double per_wave = 4.0 * device_sm_count_current();
+  const double ctas_heads = std::ceil(double(nct > 8 ? rows : pl.n_heads) / 4.0);
+  const double rounds_heads = std::ceil(spans / in_flight) * std::ceil(ctas_heads / per_wave);
+  const double rounds_split = (std::ceil(spans / 64.0) + 1.0) * std::ceil(double(rows) / per_wave);
   if (rounds_heads <= rounds_split) {
     switch (nct) {
       case 1: return launch_reduce_heads<T, D, 1>(p, pl.n_heads, s, pdl);
@@ -511,13 +545,11 @@ cudaError_t launch_reduce_d(const pab::DecodeParams& p, const Plan& pl, cudaStre
       case 4: return launch_reduce_heads<T, D, 4>(p, pl.n_heads, s, pdl);
       case 8: return launch_reduce_heads<T, D, 8>(p, pl.n_heads, s, pdl);
       default: {  // G*D > 1024: one warp per (head, query head) row
-        const int64_t rows = int64_t(pl.n_heads) * pl.G;
         LaunchCfg lc(dim3(static_cast<unsigned>((rows + 3) / 4)), dim3(128), 0, s, pdl);
         return cudaLaunchKernelEx(&lc.cfg, pab::reduce_rows_kernel<T, D>, p);
       }
     }
   }
-  const int64_t rows = int64_t(pl.n_heads) * pl.G;
   LaunchCfg lc(dim3(static_cast<unsigned>(rows)), dim3(128), 0, s, pdl);
   return cudaLaunchKernelEx(&lc.cfg, pab::reduce_split_kernel<T, D>, p);
 }
