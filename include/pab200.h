@@ -298,6 +298,22 @@ int pab200_exchange_merge(const float* state, void* const* bufs, int32_t rank,
                           void* out, int64_t out_stride_row, int32_t out_dtype,
                           int64_t wait_limit_ns, uint32_t* status, void* stream);
 
+/* Context split across GPUs, decode and exchange in one call: the same as
+ * pab200_decode(args) in state mode followed by pab200_exchange_merge() of
+ * that state, with the reduce kernel of the decode folded into the exchange
+ * kernel (each exchange block first merges the partial states of its own
+ * rows whose heads the decode split, then exchanges).  One launch fewer and
+ * no separate merge pass per call.  args->state_o / state_lse must be this
+ * rank's packed state (lse stored right after o, the layout
+ * pab200_exchange_merge() reads); `workspace` and the exchange arguments
+ * follow pab200_decode() and pab200_exchange_merge().  The reference has no
+ * multi-device code: this replaces an all-gather of the states followed by
+ * the reduce of src/kernel_triton.py:120-174 applied across devices. */
+int pab200_decode_exchange(const pab200_decode_args* args, void* workspace,
+                           size_t workspace_bytes, void* const* bufs, int32_t rank,
+                           int32_t world, void* out, int64_t out_stride_row, int32_t out_dtype,
+                           int64_t wait_limit_ns, uint32_t* status, void* stream);
+
 /* Arguments of pab200_kv_append(): the step before a decode, writing each
  * (sequence, kv head)'s new token into its page.  Cache layout, block-table
  * addressing and seqlens strides mean what they mean in pab200_decode_args. */

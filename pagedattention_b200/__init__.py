@@ -13,6 +13,7 @@ from .kernel_b200 import (
     merge_packed_states,
     merge_states,
     paged_attention,
+    paged_attention_exchange,
     paged_attention_states,
     read_status,
     state_numel,
@@ -27,6 +28,7 @@ __all__ = [
     "merge_packed_states",
     "merge_states",
     "paged_attention",
+    "paged_attention_exchange",
     "paged_attention_states",
     "read_status",
     "state_numel",

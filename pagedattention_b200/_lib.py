@@ -58,6 +58,7 @@ EXPORTED_SYMBOLS = (
     "pab200_exchange_buffer_close",
     "pab200_exchange_buffer_destroy",
     "pab200_exchange_merge",
+    "pab200_decode_exchange",
     "pab200_read_status",
     "pab200_strerror",
     "pab200_last_error",
@@ -198,6 +199,11 @@ def load() -> ctypes.CDLL:
         ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64,
         ctypes.c_void_p, ctypes.c_void_p]
     lib.pab200_exchange_merge.restype = ctypes.c_int
+    lib.pab200_decode_exchange.argtypes = [
+        P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_void_p]
+    lib.pab200_decode_exchange.restype = ctypes.c_int
     lib.pab200_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32),
                                        ctypes.c_void_p]
     lib.pab200_read_status.restype = ctypes.c_int

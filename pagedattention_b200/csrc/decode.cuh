@@ -1584,15 +1584,18 @@ __global__ void __launch_bounds__(128) reduce_heads_kernel(const DecodeParams p)
   }
 }
 
-// reduce_rows_kernel: one warp per (head, query head) row, 16 partials'
-// loads in flight per step; for large query groups (G * D > 1024) whose heads
-// hold few partials.  4 warps per CTA.
+// reduce_rows_kernel: one warp per (head, query head) row — at D = 64 one
+// half-warp per row, since a row is 16 float4 chunks — 16 partials' loads in
+// flight per step; for large query groups (G * D > 1024) whose heads hold
+// few partials.  4 warps per CTA.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) reduce_rows_kernel(const DecodeParams p) {
+  constexpr int RPW = D < 128 ? 128 / D : 1;  // rows per warp
   const int lane = threadIdx.x & 31;
+  const int sub = lane % (32 / RPW);          // lane within the row's lanes
   const int G = p.G;
   const int rows = p.B * p.Hkv * G;
-  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int r = (blockIdx.x * 4 + (threadIdx.x >> 5)) * RPW + lane / (32 / RPW);
   const uint32_t par = reduce_prologue(p);
   if (r >= rows) return;
   const int hd = r / G, g = r - hd * G;
@@ -1602,8 +1605,8 @@ __global__ void __launch_bounds__(128) reduce_rows_kernel(const DecodeParams p) 
   const int g1[1] = {g}, a1[1] = {0}, b1[1] = {hs.y};
   float M[1], L[1];
   float4 acc[1][(D + 127) / 128];
-  fold_rows<D, 1, 16>(bs1, g1, a1, b1, p.slot_floats, G, lane, M, L, acc);
-  write_row<T, D>(p, hd, g, lane, M[0], L[0], acc[0]);
+  fold_rows<D, 1, 16>(bs1, g1, a1, b1, p.slot_floats, G, sub, M, L, acc);
+  write_row<T, D>(p, hd, g, sub, M[0], L[0], acc[0]);
 }
 
 // reduce_split_kernel: one CTA of 4 warps per row; warp w folds partials
@@ -1813,7 +1816,7 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const AppendParams p) {
 // ahead because its next call waits for this rank's words of the call in
 // between, which this rank stores only after finishing the current one.
 struct ExchangeParams {
-  const float* state;       // this rank's packed state: o [rows, D], lse [rows]
+  float* state;             // this rank's packed state: o [rows, D], lse [rows]
   uint64_t* const* bufs;    // [world] exchange buffers as mapped here (bufs[rank] own)
   int32_t rank, world;
   int64_t S;                // floats per packed state (multiple of 4)
@@ -1824,6 +1827,16 @@ struct ExchangeParams {
   int64_t out_stride;
   uint64_t wait_limit_ns;
   uint32_t* status;         // PAB200_STATUS_* bits (timeout)
+  // Fused with the decode call that wrote `state` (part != nullptr): the
+  // rows of heads that call split over several segments are still partial
+  // states in its workspace; each block first folds its own rows' partials
+  // into `state` (the reduce kernel's merge, in this kernel), then exchanges.
+  // Row r is query head r % G of head r / G.
+  const float* part;
+  const int4* hseg;
+  const uint32_t* parity;
+  int32_t slot_floats;
+  int32_t G;
 };
 
 __host__ __device__ inline int64_t exchange_blocks(int64_t rows) {
@@ -1868,7 +1881,7 @@ __device__ __forceinline__ void ll_load(const uint64_t* p, int64_t step, uint32_
   for (int k = 0; k < N; ++k) v[k] = __uint_as_float(static_cast<uint32_t>(w[k]));
 }
 
-template <typename TO>
+template <typename TO, int DF>
 __global__ void __launch_bounds__(256) exchange_merge_kernel(const ExchangeParams p) {
   const int world = p.world, rank = p.rank;
   const int64_t S = p.S, rows = p.rows;
@@ -1877,12 +1890,44 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const ExchangeParam
   const int64_t r0 = b * p.rows_per_block;
   const int64_t r1 = r0 + p.rows_per_block < rows ? r0 + p.rows_per_block : rows;
   uint32_t* epochs = reinterpret_cast<uint32_t*>(p.bufs[rank] + 2 * world * S);
-  // `state` (and, after a previous exchange, `epochs`) were written by the
-  // preceding grid on this stream: read them only after it has completed.
-  // The next call's planner may then start: it writes nothing this kernel
-  // reads, and it waits for this kernel before it completes.
-  grid_dependency_wait();
+  // The next call's planner may start at once: it writes nothing before
+  // this grid has finished.  `state` (and, after a previous exchange,
+  // `epochs`) were written by the preceding grid on this stream: read them
+  // only after it has completed.
   grid_launch_dependents();
+  grid_dependency_wait();
+  if constexpr (DF > 0) {
+    // 0. fused with the decode call: fold the split heads' partial states of
+    //    rows [r0, r1) into `state`, one warp per row, in slot order (the
+    //    reduce kernels' merge); rows of whole or empty heads were written
+    //    by the decode grid already.
+    if (p.part) {
+      const int lane = tid & 31;
+      const uint32_t hpar = *reinterpret_cast<const volatile uint32_t*>(p.parity) & 1u;
+      for (int64_t row = r0 + (tid >> 5); row < r1; row += blockDim.x / 32) {
+        const int hd = static_cast<int>(row / p.G), g = static_cast<int>(row - int64_t(hd) * p.G);
+        const int4 h4 = p.hseg[hd];
+        const int2 hs = hpar ? make_int2(h4.z, h4.w) : make_int2(h4.x, h4.y);
+        if (hs.y <= 1) continue;
+        const float* bs1[1] = {p.part + static_cast<int64_t>(hd + hs.x) * p.slot_floats};
+        const int g1[1] = {g}, a1[1] = {0}, b1[1] = {hs.y};
+        float M[1], L[1];
+        float4 acc[1][(DF + 127) / 128];
+        fold_rows<DF, 1, 16>(bs1, g1, a1, b1, p.slot_floats, p.G, lane, M, L, acc);
+        const float inv = 1.f / L[0];
+#pragma unroll
+        for (int i = 0; i < (DF + 127) / 128; ++i) {
+          const int c = lane * 4 + 128 * i;
+          if (c < DF)
+            *reinterpret_cast<float4*>(p.state + row * DF + c) =
+                make_float4(acc[0][i].x * inv, acc[0][i].y * inv, acc[0][i].z * inv,
+                            acc[0][i].w * inv);
+        }
+        if (lane == 0) p.state[rows * DF + row] = (M[0] + __log2f(L[0])) * kLn2;
+      }
+      __syncthreads();  // the block's rows are final before they are sent
+    }
+  }
   const uint32_t e = reinterpret_cast<volatile uint32_t*>(epochs)[b] + 1u;
   const int par = e & 1;
   // 1. store rows [r0, r1) of o and lse into every peer's slot [par][rank]

@@ -535,7 +535,8 @@ cudaError_t launch_reduce_d(const pab::DecodeParams& p, const Plan& pl, cudaStre
   const double in_flight = nct > 8 ? 16.0 : 16.0 / nct;
   const int64_t rows = int64_t(pl.n_heads) * pl.G;
   const double per_wave = 4.0 * device_sm_count_current();
-  const double ctas_heads = std::ceil(double(nct > 8 ? rows : pl.n_heads) / 4.0);
+  const double ctas_heads =
+      std::ceil(double(nct > 8 ? rows : pl.n_heads) / (nct > 8 && D < 128 ? 4.0 * (128 / D) : 4.0));
   const double rounds_heads = std::ceil(spans / in_flight) * std::ceil(ctas_heads / per_wave);
   const double rounds_split = (std::ceil(spans / 64.0) + 1.0) * std::ceil(double(rows) / per_wave);
   if (rounds_heads <= rounds_split) {
@@ -544,8 +545,10 @@ cudaError_t launch_reduce_d(const pab::DecodeParams& p, const Plan& pl, cudaStre
       case 2: return launch_reduce_heads<T, D, 2>(p, pl.n_heads, s, pdl);
       case 4: return launch_reduce_heads<T, D, 4>(p, pl.n_heads, s, pdl);
       case 8: return launch_reduce_heads<T, D, 8>(p, pl.n_heads, s, pdl);
-      default: {  // G*D > 1024: one warp per (head, query head) row
-        LaunchCfg lc(dim3(static_cast<unsigned>((rows + 3) / 4)), dim3(128), 0, s, pdl);
+      default: {  // G*D > 1024: one warp (D = 64: half-warp) per (head, query head) row
+        const int64_t per_cta = D < 128 ? 4 * (128 / D) : 4;
+        LaunchCfg lc(dim3(static_cast<unsigned>((rows + per_cta - 1) / per_cta)), dim3(128), 0, s,
+                     pdl);
         return cudaLaunchKernelEx(&lc.cfg, pab::reduce_rows_kernel<T, D>, p);
       }
     }
@@ -577,10 +580,15 @@ PAB200_EXPORT int pab200_decode_launch_count(const pab200_decode_args* args) {
 }
 
 namespace {
+cudaError_t launch_exchange(const pab::ExchangeParams& p, int out_dtype, int fused_d,
+                            cudaStream_t s);
+
 // One decode call planned as `pl`; with `app`, the planner first appends the
-// step's tokens.
+// step's tokens; with `exchange`, the call ends in the fused exchange + merge
+// of a context split across GPUs instead of the reduce kernel.
 int decode_impl(const pab200_decode_args* a, const Plan& pl, const pab::AppendParams* app,
-                void* workspace, size_t workspace_bytes, void* stream) {
+                void* workspace, size_t workspace_bytes, void* stream,
+                pab::ExchangeParams* exchange = nullptr, int exchange_dtype = 0) {
   int rc = PAB200_OK;
   if (!workspace || workspace_bytes < pl.ws_bytes)
     return fail(PAB200_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", pl.ws_bytes,
@@ -669,6 +677,19 @@ int decode_impl(const pab200_decode_args* a, const Plan& pl, const pab::AppendPa
   if (a->event_after) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a->event_after), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  if (exchange) {
+    // Context split across GPUs: the exchange + merge kernel folds the split
+    // heads' partial states itself (no reduce kernel).
+    exchange->part = p.part;
+    exchange->hseg = p.hseg;
+    exchange->parity = p.parity;
+    exchange->slot_floats = p.slot_floats;
+    exchange->G = p.G;
+    e = launch_exchange(*exchange, exchange_dtype, p.D, s);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "exchange kernel launch");
+    return PAB200_OK;
   }
   const bool pdl_r = pdl && !a->event_after;
   e = a->dtype == PAB200_DTYPE_BF16 ? launch_reduce<__nv_bfloat16>(p, pl, s, pdl_r)
@@ -901,57 +922,98 @@ PAB200_EXPORT int pab200_exchange_buffer_destroy(void* buf) {
   return e == cudaSuccess ? PAB200_OK : cuda_fail(e, "cudaFree");
 }
 
-PAB200_EXPORT int pab200_exchange_merge(const float* state, void* const* bufs, int32_t rank,
-                                        int32_t world, int64_t rows, int32_t head_size, void* out,
-                                        int64_t out_stride_row, int32_t out_dtype,
-                                        int64_t wait_limit_ns, uint32_t* status, void* stream) {
+namespace {
+// Checks the arguments of an exchange + merge and fills its parameters
+// (without the fused-decode fields).
+int exchange_params(float* state, void* const* bufs, int32_t rank, int32_t world, int64_t rows,
+                    int32_t head_size, void* out, int64_t out_stride_row, int32_t out_dtype,
+                    int64_t wait_limit_ns, uint32_t* status, pab::ExchangeParams* p) {
   if (world < 1 || world > 64 || rank < 0 || rank >= world || rows < 1 || head_size < 4 ||
       (head_size & 3) || wait_limit_ns <= 0)
     return fail(PAB200_ERR_INVALID_ARGUMENT,
                 "need 0 <= rank < world <= 64, rows >= 1, head_size %% 4 == 0, wait_limit_ns > 0");
   if (!state || !bufs || !out || !status) return fail(PAB200_ERR_INVALID_ARGUMENT, "null pointer");
+  if (out_dtype != PAB200_DTYPE_BF16 && out_dtype != PAB200_DTYPE_F16 && out_dtype != PAB200_DTYPE_F32)
+    return fail(PAB200_ERR_UNSUPPORTED, "out_dtype %d", out_dtype);
   const size_t oal = out_dtype == PAB200_DTYPE_F32 ? 16 : 8;
   if (!aligned(state, 16) || !aligned(out, oal) || (out_stride_row & 3) || !aligned(status, 4))
     return fail(PAB200_ERR_ALIGNMENT, "state 16-byte, out %zu-byte aligned, out_stride_row %% 4 == 0",
                 oal);
-  pab::ExchangeParams p{};
-  p.state = state;
-  p.bufs = reinterpret_cast<uint64_t* const*>(bufs);
-  p.rank = rank;
-  p.world = world;
-  p.S = packed_state_floats(rows, head_size);
-  p.rows = rows;
-  p.D = head_size;
-  p.out = out;
-  p.out_stride = out_stride_row;
-  p.wait_limit_ns = static_cast<uint64_t>(wait_limit_ns);
-  p.status = status;
+  *p = pab::ExchangeParams{};
+  p->state = state;
+  p->bufs = reinterpret_cast<uint64_t* const*>(bufs);
+  p->rank = rank;
+  p->world = world;
+  p->S = packed_state_floats(rows, head_size);
+  p->rows = rows;
+  p->D = head_size;
+  p->out = out;
+  p->out_stride = out_stride_row;
+  p->wait_limit_ns = static_cast<uint64_t>(wait_limit_ns);
+  p->status = status;
   // Every rank uses the same grid: block b owns rows [b*rpb, (b+1)*rpb) on
   // all ranks and waits only for the peers' block b.
   const int64_t blocks = pab::exchange_blocks(rows);
-  p.rows_per_block = (rows + blocks - 1) / blocks;
-  // Programmatic dependent launch: the grid is scheduled while the kernel
-  // that writes `state` drains, and waits for it (griddepcontrol.wait)
-  // before the first read.
-  LaunchCfg lc(dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
-               static_cast<cudaStream_t>(stream), true);
-  cudaError_t e;
-  switch (out_dtype) {
-    case PAB200_DTYPE_BF16:
-      e = cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<__nv_bfloat16>, p);
-      break;
-    case PAB200_DTYPE_F16:
-      e = cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<__half>, p);
-      break;
-    case PAB200_DTYPE_F32:
-      e = cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<float>, p);
-      break;
-    default:
-      return fail(PAB200_ERR_UNSUPPORTED, "out_dtype %d", out_dtype);
+  p->rows_per_block = (rows + blocks - 1) / blocks;
+  return PAB200_OK;
+}
+
+// Programmatic dependent launch: the grid is scheduled while the kernel
+// that writes `state` drains, and waits for it (griddepcontrol.wait) before
+// the first read.  fused_d: 0, or the head size when the kernel first folds
+// the split heads' partial states of the decode call before it.
+template <typename TO>
+cudaError_t launch_exchange_t(const pab::ExchangeParams& p, int fused_d, cudaStream_t s) {
+  LaunchCfg lc(dim3(static_cast<unsigned>(pab::exchange_blocks(p.rows))), dim3(256), 0, s, true);
+  switch (fused_d) {
+    case 0: return cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<TO, 0>, p);
+    case 64: return cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<TO, 64>, p);
+    case 128: return cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<TO, 128>, p);
+    default: return cudaLaunchKernelEx(&lc.cfg, pab::exchange_merge_kernel<TO, 256>, p);
   }
+}
+
+cudaError_t launch_exchange(const pab::ExchangeParams& p, int out_dtype, int fused_d,
+                            cudaStream_t s) {
+  switch (out_dtype) {
+    case PAB200_DTYPE_BF16: return launch_exchange_t<__nv_bfloat16>(p, fused_d, s);
+    case PAB200_DTYPE_F16: return launch_exchange_t<__half>(p, fused_d, s);
+    default: return launch_exchange_t<float>(p, fused_d, s);
+  }
+}
+}  // namespace
+
+PAB200_EXPORT int pab200_exchange_merge(const float* state, void* const* bufs, int32_t rank,
+                                        int32_t world, int64_t rows, int32_t head_size, void* out,
+                                        int64_t out_stride_row, int32_t out_dtype,
+                                        int64_t wait_limit_ns, uint32_t* status, void* stream) {
+  pab::ExchangeParams p;
+  const int rc = exchange_params(const_cast<float*>(state), bufs, rank, world, rows, head_size, out,
+                                 out_stride_row, out_dtype, wait_limit_ns, status, &p);
+  if (rc) return rc;
+  cudaError_t e = launch_exchange(p, out_dtype, 0, static_cast<cudaStream_t>(stream));
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "exchange kernel launch");
   return PAB200_OK;
+}
+
+PAB200_EXPORT int pab200_decode_exchange(const pab200_decode_args* a, void* workspace,
+                                         size_t workspace_bytes, void* const* bufs, int32_t rank,
+                                         int32_t world, void* out, int64_t out_stride_row,
+                                         int32_t out_dtype, int64_t wait_limit_ns,
+                                         uint32_t* status, void* stream) {
+  if (!a) return fail(PAB200_ERR_INVALID_ARGUMENT, "args is null");
+  const int64_t rows = int64_t(a->num_seqs) * a->num_q_heads;
+  if (!a->state_o || !a->state_lse || a->state_lse != a->state_o + rows * a->head_size)
+    return fail(PAB200_ERR_INVALID_ARGUMENT,
+                "state_o / state_lse must be this rank's packed state (lse right after o)");
+  pab::ExchangeParams ep;
+  int rc = exchange_params(a->state_o, bufs, rank, world, rows, a->head_size, out, out_stride_row,
+                           out_dtype, wait_limit_ns, status, &ep);
+  if (rc) return rc;
+  Plan pl;
+  if ((rc = make_plan(a, &pl, SIZE_MAX))) return rc;
+  return decode_impl(a, pl, nullptr, workspace, workspace_bytes, stream, &ep, out_dtype);
 }
 
 namespace {

@@ -18,7 +18,10 @@ The decode path spreads over devices in two ways:
   output is the full-context result.  With a ``PeerExchange`` the gather and
   the merge are one kernel over peer memory instead (NVLink stores into
   every rank's exchange buffer, mapped with CUDA IPC; an epoch flag per rank;
-  a bounded wait), which saves the NCCL launch and the separate merge.
+  a bounded wait), launched by the decode call itself in place of its reduce
+  kernel (``paged_attention_exchange``: the exchange kernel also folds the
+  heads the decode split), which saves the NCCL launch, the reduce launch
+  and the separate merge.
 
 The reference has no multi-device code; this module is new.
 """
@@ -31,7 +34,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .kernel_b200 import merge_packed_states, paged_attention_states, state_numel
+from .kernel_b200 import (merge_packed_states, paged_attention_exchange, paged_attention_states,
+                          state_numel)
 
 _OUT_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16,
                torch.float32: _lib.DTYPE_F32}
@@ -261,14 +265,11 @@ def decode_context_parallel(query, key_cache, value_cache, block_tables, context
     """
     B, Hq, D = query.shape
     if exchange is not None:
-        state = exchange.state
-    else:
-        state = torch.empty(state_numel(B, Hq, D), dtype=torch.float32, device=query.device)
+        # decode, fold and exchange in one call (pab200_decode_exchange)
+        return paged_attention_exchange(query, key_cache, value_cache, block_tables, context_lens,
+                                        scale, block_size, exchange, out=out, kv_layout=kv_layout)
+    state = torch.empty(state_numel(B, Hq, D), dtype=torch.float32, device=query.device)
     paged_attention_states(query, key_cache, value_cache, block_tables, context_lens, scale,
                            block_size, kv_layout=kv_layout, state=state)
-    if exchange is not None:
-        if out is None:
-            out = torch.empty((B, Hq, D), dtype=query.dtype, device=query.device)
-        return exchange.exchange_merge(state, out)
     gathered = all_gather_states(state, group)
     return merge_packed_states(gathered, B, Hq, D, out=out, out_dtype=query.dtype)

@@ -128,17 +128,17 @@ def kernel_events(before: torch.cuda.Event, after: torch.cuda.Event):
         _tls.events = prev
 
 
-def _run_decode(args: _lib.DecodeArgs, device: torch.device, append=None) -> None:
+def _run_decode(args: _lib.DecodeArgs, device: torch.device, append=None, exchange=None) -> None:
     lib = _lib.load()
     ev = getattr(_tls, "events", None)
     if ev is not None:
         args.event_before = ev[0].cuda_event
         args.event_after = ev[1].cuda_event
     if torch.cuda.current_device() == device.index:
-        rc = _launch(lib, args, device, append)
+        rc = _launch(lib, args, device, append, exchange)
     else:
         with torch.cuda.device(device):
-            rc = _launch(lib, args, device, append)
+            rc = _launch(lib, args, device, append, exchange)
     if rc == _lib.ERR_INVALID_ARGUMENT or rc == _lib.ERR_UNSUPPORTED:
         raise ValueError(f"pab200_decode: {_lib.error_text(lib, rc)}")
     _lib.check(lib, rc, "pab200_decode")
@@ -153,20 +153,28 @@ def _current_stream_handle(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def _call(lib, args, append, ws, stream_handle) -> int:
+def _call(lib, args, append, ws, stream_handle, exchange=None) -> int:
+    if exchange is not None:
+        ex, out, code = exchange
+        return lib.pab200_decode_exchange(
+            ctypes.byref(args), ws.data_ptr(), ws.numel(), ex.bufs.data_ptr(), ex.rank, ex.world,
+            out.data_ptr(), out.stride(1), code, ex.wait_limit_ns, ex.status.data_ptr(),
+            stream_handle)
     if append is None:
         return lib.pab200_decode(ctypes.byref(args), ws.data_ptr(), ws.numel(), stream_handle)
     return lib.pab200_decode_append(ctypes.byref(args), ctypes.byref(append), ws.data_ptr(),
                                     ws.numel(), stream_handle)
 
 
-def _launch(lib, args, device, append=None) -> int:
+def _launch(lib, args, device, append=None, exchange=None) -> int:
     stream_handle = _current_stream_handle(device)
-    rc = _call(lib, args, append, _workspace(lib, args, device, stream_handle), stream_handle)
+    rc = _call(lib, args, append, _workspace(lib, args, device, stream_handle), stream_handle,
+               exchange)
     if rc == _lib.ERR_WORKSPACE:
         # launch geometry changed (e.g. a tuning variable): re-size once
         _ws_sizes.clear()
-        rc = _call(lib, args, append, _workspace(lib, args, device, stream_handle), stream_handle)
+        rc = _call(lib, args, append, _workspace(lib, args, device, stream_handle),
+                   stream_handle, exchange)
     return rc
 
 
@@ -433,6 +441,42 @@ def paged_attention_states(query, key_cache, value_cache, block_tables, context_
     _run_decode(args, device)
     del keep
     return o, lse
+
+
+def paged_attention_exchange(query, key_cache, value_cache, block_tables, context_lens, scale,
+                             block_size, exchange, out=None, kv_layout="HND", num_splits=0):
+    """Decode this rank's token ranges and merge every rank's result (a
+    context split across the GPUs of one node), in one call.
+
+    Arguments as for ``paged_attention_states``; ``exchange`` is a
+    ``PeerExchange`` of this shape.  The decode writes this rank's (o, lse)
+    state into ``exchange.state`` and the exchange kernel, which also folds
+    the partial states of heads the decode split, stores it into every
+    peer's buffer and merges the world's states into ``out`` (num_seqs,
+    num_q_heads, head_size) in query's dtype, identical on every rank.  The
+    log-sum-exp merge is the reduce of src/kernel_triton.py:120-174 applied
+    across devices.
+    """
+    args, device, keep = _paged_args(query, key_cache, value_cache, block_tables, context_lens,
+                                     scale, block_size, kv_layout, num_splits)
+    B, Hq, D = query.shape
+    if (B, Hq, D) != tuple(exchange.shape):
+        raise ValueError(f"query shape {(B, Hq, D)} != exchange shape {tuple(exchange.shape)}")
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=query.dtype, device=device)
+    code = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16,
+            torch.float32: _lib.DTYPE_F32}.get(out.dtype)
+    if code is None:
+        raise TypeError(f"unsupported out dtype {out.dtype}")
+    if tuple(out.shape) != (B, Hq, D) or not out.is_contiguous() or out.device != device:
+        raise ValueError(f"out must be a contiguous {(B, Hq, D)} tensor on {device}")
+    rows = B * Hq
+    state = exchange.state
+    args.state_o = state.data_ptr()
+    args.state_lse = state.data_ptr() + rows * D * 4
+    _run_decode(args, device, exchange=(exchange, out, code))
+    del keep
+    return out
 
 
 def _merge(lib, device, o_ptr, o_stride, lse_ptr, lse_stride, n, rows, D, out):

@@ -156,6 +156,17 @@ def test_exchange_argument_checks():
     assert lib.pab200_exchange_merge(*args) == _lib.ERR_INVALID_ARGUMENT
     args = (8, 16, 0, 2, rows, D, 16, D, _lib.DTYPE_BF16, 10**9, 16, None)
     assert lib.pab200_exchange_merge(*args) == _lib.ERR_ALIGNMENT
+    # the fused decode + exchange: args and the packed state are checked first
+    assert lib.pab200_decode_exchange(None, 0, 0, 16, 0, 2, 16, D, _lib.DTYPE_BF16, 10**9, 16,
+                                      None) == _lib.ERR_INVALID_ARGUMENT
+    a = _lib.DecodeArgs()
+    a.num_seqs, a.num_q_heads, a.head_size = 2, 4, D
+    a.state_o, a.state_lse = 256, 256 + 4            # lse not right after o
+    assert lib.pab200_decode_exchange(ctypes.byref(a), 0, 0, 16, 0, 2, 16, D, _lib.DTYPE_BF16,
+                                      10**9, 16, None) == _lib.ERR_INVALID_ARGUMENT
+    a.state_lse = 256 + 2 * 4 * D * 4                # packed, but rank outside [0, world)
+    assert lib.pab200_decode_exchange(ctypes.byref(a), 0, 0, 16, 2, 2, 16, D, _lib.DTYPE_BF16,
+                                      10**9, 16, None) == _lib.ERR_INVALID_ARGUMENT
     assert lib.pab200_exchange_buffer_close(None) == _lib.OK
     assert lib.pab200_exchange_buffer_destroy(None) == _lib.OK
     assert lib.pab200_exchange_buffer_create(0, ctypes.byref(ctypes.c_void_p()), None) == \
