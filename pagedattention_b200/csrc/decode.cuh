@@ -58,6 +58,8 @@
 //   bank-conflict free.
 #pragma once
 
+#include <type_traits>
+
 #include "ptx.cuh"
 
 namespace pab {
@@ -77,6 +79,23 @@ constexpr int kCoreMaxG = 4;           // largest query group of the CUDA-core p
 // kv head) pairs keep their page-count prefix in shared memory.
 constexpr int kEarlyMaxHeads = 1024;
 constexpr int kEarlyBytes = (2 * kEarlyMaxHeads + 1 + 32) * 4;  // cum, lengths, warp sums
+
+// tcgen05 path (query groups of up to 32 heads, D 64, 64-token stages): a
+// unit of two warps per ring; tensor-memory columns per unit (two score
+// buffers of 32 columns, the 64-column output accumulator); bytes of one
+// 64-row x 128-byte operand tile (queries, or probabilities).
+constexpr int kTcUnitCols = 128;
+constexpr int kTcTileBytes = 64 * 128;
+// Offsets, from the start of the tail (after the paired layout's stage
+// mbarriers, stage records and slot-free mbarriers), of the tcgen05 path's
+// per-unit mbarriers and of the tensor-memory base address.
+constexpr int kTcBarsPerUnit = 6;
+__host__ __device__ constexpr int tc_bars_offset(int upc) {
+  return upc * kMaxDepth * (8 + kMetaBytesPerSlot) + upc * kMaxDepth * 8;
+}
+__host__ __device__ constexpr int tc_slot_offset(int upc) {
+  return tc_bars_offset(upc) + upc * kTcBarsPerUnit * 8;
+}
 
 // Per-warp shared memory of the CUDA-core path: the query group in fp32.
 __host__ __device__ constexpr int core_q_bytes(bool core, int D) {
@@ -431,6 +450,12 @@ __global__ void __launch_bounds__(1024) plan_kernel(const DecodeParams p) {
 
 // --------------------------------------------------------------------------
 // Shared-memory helpers of the CUDA-core path.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -585,8 +610,8 @@ __device__ __forceinline__ void write_row(const DecodeParams& p, int hd, int g, 
 // group of up to 32 query heads fits at D = 128.  (At D = 64 the pair runs
 // twice the resident warps of the single-warp kernel but is slower: each
 // stage waits on both warps, and the per-stage issue work does not split.)
-template <typename T, int D, int NT, int ST, bool CORE, bool PAIR = false>
-__global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 1)
+template <typename T, int D, int NT, int ST, bool CORE, bool PAIR = false, bool TC = false>
+__global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64 && !TC) ? 2 : 1)
     decode_kernel(const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap,
                   const DecodeParams p) {
@@ -603,6 +628,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   constexpr int DL = D / 32;  // head-dim elements per lane (CUDA-core path)
   static_assert(NH == 1 || NH == 2 || NH == 4, "head size");
   static_assert(!(CORE && PAIR), "the CUDA-core path has no paired variant");
+  static_assert(!TC || (PAIR && !CORE && D == 64 && ST == 64 && NT == 2), "tcgen05 path shape");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -621,6 +647,26 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   const int gw = blockIdx.x * upc + unit;
   const int g_lo = PAIR ? role * NT * 8 : 0;  // first query head of this warp
   const int n_heads = p.B * p.Hkv;
+  // tcgen05 path: the query and probability tiles (shared by the two units
+  // of a unit pair) follow the rings; the tail (mbarriers, stage records)
+  // follows them.  Tensor memory is allocated once per CTA here, before any
+  // early exit, and freed at the end of the kernel by the same warp after a
+  // CTA barrier that every warp reaches.
+  const int tc_tiles = TC ? ((upc + 1) / 2) * 2 * kTcTileBytes : 0;
+  uint8_t* const tail0 = smem + upc * depth * STAGE_BYTES + tc_tiles;
+  uint32_t tbase = 0;
+  const uint32_t tc_cols = upc > 2 ? 512u : static_cast<uint32_t>(upc) * kTcUnitCols;
+  if constexpr (TC) {
+    const uint32_t slot = smem_addr(tail0) + tc_slot_offset(upc);
+    if (warp == 0) {
+      tmem_alloc(slot, tc_cols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tbase = *reinterpret_cast<volatile uint32_t*>(tail0 + tc_slot_offset(upc));
+  }
   // The reduce grid may be scheduled at once: it waits for this grid to
   // complete before it reads anything.
   grid_launch_dependents();
@@ -656,8 +702,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   // alike, so ranges, tail chunks and segments agree.
   const bool early = !PAIR && p.early != 0;
   int* const cum_sm = reinterpret_cast<int*>(
-      smem + upc * depth * STAGE_BYTES + upc * kMaxDepth * (8 + kMetaBytesPerSlot) +
-      upc * core_q_bytes(CORE, D));
+      tail0 + upc * kMaxDepth * (8 + kMetaBytesPerSlot) + upc * core_q_bytes(CORE, D));
   int* const len_sm = cum_sm + kEarlyMaxHeads + 1;
   int W, total, first_head = 0, sm_m, sm_k;
   if (early) {
@@ -709,12 +754,15 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   }
   const int gs = gw < W ? static_cast<int>(static_cast<int64_t>(gw) * total / W) : 0;
   const int g_end = gw < W ? static_cast<int>(static_cast<int64_t>(gw + 1) * total / W) : 0;
-  if (gw >= W || total == 0 || gs >= g_end) {
+  // A unit without pages leaves (the tcgen05 path keeps it to the end, where
+  // the CTA frees its tensor memory).
+  const bool idle = gw >= W || total == 0 || gs >= g_end;
+  if (idle) {
     if (early) {
       grid_dependency_wait();
       zero_empty_heads();
     }
-    return;
+    if constexpr (!TC) return;
   }
   // Current segment [c_gp, ge): the static prefix first, then tail chunks
   // claimed from the front of this warp's tail, then chunks stolen from the
@@ -731,7 +779,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   const int pps = 1 << log2_pps;
   const int cap = p.maxb << log2_bs;
   const uint32_t ring = smem_base + unit * depth * STAGE_BYTES;
-  uint8_t* tail = smem + upc * depth * STAGE_BYTES;
+  uint8_t* tail = tail0;
   const uint32_t bars = smem_addr(tail) + unit * kMaxDepth * 8;
   int4* meta = reinterpret_cast<int4*>(tail + upc * kMaxDepth * 8) +
                unit * kMaxDepth * 2;
@@ -741,10 +789,24 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   const uint32_t empties = smem_addr(tail) + upc * kMaxDepth * (8 + kMetaBytesPerSlot) +
                            upc * core_q_bytes(CORE, D) + unit * kMaxDepth * 8;
 
+  // tcgen05 path, per unit: scores of even / odd stages ready (MMA
+  // commit), probabilities-times-V of a stage done (MMA commit; frees the
+  // probability tile, the stage's ring slot and the output accumulator),
+  // probabilities written (one arrival per warp), and one drain barrier per
+  // warp (MMA commit).
+  const uint32_t tcb = smem_addr(tail) + tc_bars_offset(upc) + unit * kTcBarsPerUnit * 8;
   if (lane == 0 && role == 0) {
     for (int i = 0; i < depth; ++i) {
       mbar_init(bars + i * 8, 1);
       if constexpr (PAIR) mbar_init(empties + i * 8, 1);
+    }
+    if constexpr (TC) {
+      mbar_init(tcb, 1);
+      mbar_init(tcb + 8, 1);
+      mbar_init(tcb + 16, 1);
+      mbar_init(tcb + 24, 2);
+      mbar_init(tcb + 32, 1);
+      mbar_init(tcb + 40, 1);
     }
     fence_mbar_init();
     tma_prefetch_desc(&kmap);
@@ -923,7 +985,11 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   bool nx_valid = false;
   int nx_head = 0, nx_h = 0, nx_lp0 = 0, nx_np = 0, nx_len = 0, nx_slot = 0, nx_vfirst = 0,
       nx_vlast = 0;
-  int64_t nx_pid = 0;  // lane i < nx_np: page id of page i of the stage
+  // lane i < nx_np: block-table entry of page i of the stage, kept as
+  // loaded (the page id is formed where it is used, one stage later, so the
+  // load's latency is not waited for here), and the head's page-id offset.
+  int32_t nx_raw = 0;
+  int64_t nx_add = 0;
   auto prepare_next = [&]() {
     if (c_gp >= ge) {
       ensure_waited();  // claims and stealing touch shared state
@@ -953,8 +1019,8 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     nx_vfirst = c_vfirst;
     nx_vlast = c_vlast;
     if (lane < np)
-      nx_pid = static_cast<int64_t>(c_bt[static_cast<int64_t>(nx_lp0 + lane) * p.bt_si]) *
-                   p.bt_mul + c_pid_add;
+      nx_raw = c_bt[static_cast<int64_t>(nx_lp0 + lane) * p.bt_si];
+    nx_add = c_pid_add;
     c_gp += np;
   };
   auto issue = [&](int slot) -> bool {
@@ -966,6 +1032,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
       mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nx_np << (log2_bs + LOG2_NH + 8)));
     }
     __syncwarp();
+    const int64_t nx_pid = static_cast<int64_t>(nx_raw) * p.bt_mul + nx_add;
     const bool bad = lane < nx_np && (nx_pid < 0 || nx_pid >= p.num_pages);
     if (__any_sync(0xffffffffu, bad)) {
       if (prewait)
@@ -1201,6 +1268,407 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
     }
     sent_end = true;
   };
+  if constexpr (TC) {
+    // ------------------------------------------- tcgen05 pipeline (a unit)
+    // Stage it: S = Q K^T on the tensor core as two 64 x 32 halves (tokens
+    // 0-31 and 32-63 of the stage), written to the lower and the upper 16
+    // lanes of every TMEM sub-partition, so that each thread of a warp owns
+    // one (query head, 32-token half) of the scores.  The warps turn them
+    // into probabilities (online softmax in fp32, log2 units) stored to the
+    // probability tile, and O += P V accumulates in TMEM (64 columns).  Lane
+    // 0 of the MMA warp issues every MMA; the scores of stage it + 1 are
+    // computed while the warps work on stage it.
+    //
+    // The MMAs have M = 64 rows: rows 0-31 belong to even units, rows 32-63
+    // to odd units (a warp reads only its own TMEM sub-partition, warp % 4;
+    // row r of an M = 64 accumulator lies in lane (r % 16) + 32 (r / 16), 16
+    // lanes higher for the upper half).  The query and probability tiles of
+    // a unit pair are shared, each unit writing its own 32 rows; the rows of
+    // the other unit only produce accumulator rows that nobody reads.
+    constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+    // Instruction descriptors: fp32 accumulate, A and B of type T, M = 64;
+    // QK^T with both operands K-major and N = 32; PV with B (V) MN-major and
+    // N = 64.
+    constexpr uint32_t kIdescQK =
+        (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((32u >> 3) << 17) | ((64u >> 4) << 24);
+    constexpr uint32_t kIdescPV = (1u << 4) | (kFmt << 7) | (kFmt << 10) | (1u << 16) |
+                                  ((64u >> 3) << 17) | ((64u >> 4) << 24);
+    // mbarriers: scores ready (two buffers), PV done, probabilities written,
+    // then one drain barrier per warp.
+    const uint32_t sfull0 = tcb, ofree = tcb + 16, pready = tcb + 24, drain = tcb + 32;
+    const uint32_t tiles = smem_base + upc * depth * STAGE_BYTES;
+    const uint32_t qtile = tiles + (unit >> 1) * kTcTileBytes;
+    const uint32_t ptile = tiles + ((upc + 1) / 2 + (unit >> 1)) * kTcTileBytes;
+    const int quad = warp & 3;
+    const uint32_t t_lane = static_cast<uint32_t>(32 * quad) << 16;
+    const uint32_t ucol = tbase + unit * kTcUnitCols;
+    const int row = 16 * quad + (lane & 15);  // this thread's row of the 64-row tiles
+    const int g_row = row - 32 * (unit & 1);  // its query head
+    const int half = lane >> 4;               // its 32 tokens of a stage
+    // Waits whose outcome the whole warp shares (the tcgen05 loads, stores
+    // and allocations below are warp-collective).
+    auto wait_w = [&](uint32_t bar, uint32_t par) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, par, kWaitLimitNs));
+    };
+    // MMA warp: this unit's 32 query rows of the tile (zeros past G).  With
+    // 16-byte aligned rows, lane l loads 16-byte chunk l % 8 of rows
+    // 4 i + l / 8 (coalesced, all loads in flight at once); otherwise each
+    // lane loads its row in 4-byte words.
+    const bool q_vec = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0 && (p.q_sb & 7) == 0 &&
+                       (p.q_sh & 7) == 0;
+    auto load_q = [&](int hd) {
+      const int s = hd / Hkv, h = hd - s * Hkv;
+      const T* qh0 = static_cast<const T*>(p.q) + s * p.q_sb + static_cast<int64_t>(h) * G * p.q_sh;
+      const int rbase = 32 * (unit & 1);
+      if (q_vec) {
+        uint4 w[8];
+        const int c = lane & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int g = 4 * i + (lane >> 3);
+          w[i] = g < G ? *reinterpret_cast<const uint4*>(qh0 + g * p.q_sh + c * 8)
+                       : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = rbase + 4 * i + (lane >> 3);
+          st_shared_v4(qtile + r * 128 + static_cast<uint32_t>((c ^ (r & 7)) << 4), w[i].x, w[i].y,
+                       w[i].z, w[i].w);
+        }
+      } else {
+        const int r = rbase + lane;
+        uint32_t w[32];
+        if (lane < G) {
+          const uint32_t* src = reinterpret_cast<const uint32_t*>(qh0 + lane * p.q_sh);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = src[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = 0u;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          st_shared_v4(qtile + r * 128 + static_cast<uint32_t>((c ^ (r & 7)) << 4), w[4 * c],
+                       w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      }
+      fence_proxy_async_smem();  // generic writes, read by the tensor core
+      __syncwarp();
+    };
+    // Shared-memory descriptors (128-byte swizzle, 8-row groups 1024 bytes
+    // apart) of the query tile, the probability tile and slot 0 of the
+    // ring; an operand at byte offset o adds o >> 4 (no carry out of the
+    // 14-bit start address: shared addresses are below 256 KB).
+    const uint64_t qdesc = smem_desc_sw128(qtile, 16, 1024);
+    const uint64_t pdesc = smem_desc_sw128(ptile, 16, 1024);
+    const uint64_t rdesc = smem_desc_sw128(ring, 16, 1024);
+    // MMA warp: S(j) = Q K(j)^T into score buffer j & 1 (K-steps of 16
+    // elements advance 32 bytes inside the swizzled rows; tokens 32-63 of
+    // the stage start 32 rows on).
+    auto issue_qk = [&](int j) {
+      const uint64_t kd = rdesc + static_cast<uint32_t>(((j % depth) * STAGE_BYTES) >> 4);
+      const uint32_t d = ucol + (j & 1) * 32;
+      if (lane == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            tc_mma_ss(d + (static_cast<uint32_t>(hf) << 20), qdesc + ks * 2,
+                      kd + (hf * 4096 + ks * 32) / 16, kIdescQK, static_cast<uint32_t>(ks));
+        tc_commit(sfull0 + (j & 1) * 8);
+      }
+      __syncwarp();
+    };
+    // MMA warp: O (+)= P V(j) (K-steps of 16 tokens: 32 bytes along the
+    // probability rows, 16 rows = 2048 bytes down V).
+    auto issue_pv = [&](int j, bool accumulate) {
+      const uint64_t vd = rdesc + static_cast<uint32_t>(((j % depth) * STAGE_BYTES + KV_BYTES) >> 4);
+      if (lane == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int kt = 0; kt < 4; ++kt)
+          tc_mma_ss(ucol + 64, pdesc + kt * 2, vd + kt * 128, kIdescPV,
+                    (accumulate || kt > 0) ? 1u : 0u);
+        tc_commit(ofree);
+      }
+      __syncwarp();
+    };
+    float m_run = -INFINITY, l_run = 0.f;  // this row's running max and this thread's sum
+    // Ends head hd's accumulation in segment `slot` (after its last PV):
+    // lanes 0-15 hold the rows of the output accumulator.
+    auto tc_finish = [&](int hd, int slot, int vfirst, int vlast) {
+      ensure_waited();
+      const float lt = l_run + __shfl_xor_sync(0xffffffffu, l_run, 16);
+      uint32_t o[64];
+      tmem_ld64(t_lane + ucol + 64, o);
+      tmem_wait_ld();
+      if (lane >= 16 || g_row >= G) return;
+      const int s = hd / Hkv, h = hd - s * Hkv;
+      const int Hq = Hkv * G, qh = h * G + g_row;
+      if (vfirst == vlast) {
+        const float inv = 1.f / lt;
+        if (p.state_o) {
+          float* dst = p.state_o + (static_cast<int64_t>(s) * Hq + qh) * D;
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            *reinterpret_cast<float4*>(dst + 4 * c) =
+                make_float4(__uint_as_float(o[4 * c]) * inv, __uint_as_float(o[4 * c + 1]) * inv,
+                            __uint_as_float(o[4 * c + 2]) * inv, __uint_as_float(o[4 * c + 3]) * inv);
+          p.state_lse[static_cast<int64_t>(s) * Hq + qh] = (m_run + __log2f(lt)) * kLn2;
+        } else {
+          T* dst = static_cast<T*>(p.out) + s * p.o_sb + qh * p.o_sh;
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            *reinterpret_cast<uint2*>(dst + 4 * c) =
+                make_uint2(pack2<T>(__uint_as_float(o[4 * c]) * inv, __uint_as_float(o[4 * c + 1]) * inv),
+                           pack2<T>(__uint_as_float(o[4 * c + 2]) * inv, __uint_as_float(o[4 * c + 3]) * inv));
+        }
+        return;
+      }
+      float* ps = p.part + static_cast<int64_t>(hd + slot) * p.slot_floats;
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        __stcg(reinterpret_cast<float4*>(ps + g_row * D + 4 * c),
+               make_float4(__uint_as_float(o[4 * c]), __uint_as_float(o[4 * c + 1]),
+                           __uint_as_float(o[4 * c + 2]), __uint_as_float(o[4 * c + 3])));
+      __stcg(ps + G * D + g_row, m_run);
+      __stcg(ps + G * D + G + g_row, lt);
+    };
+
+    // Roles: warp 0 of the unit loads the queries and issues every MMA;
+    // warp 1 produces the stages (schedule, tail-chunk claims, copies, stage
+    // records) and refills the slot the previous PV freed after publishing
+    // its probability rows, so that the refill overlaps the MMAs.  Both
+    // compute the softmax of their 32 rows.
+    const bool producer = role == 1;
+    bool failed = false;
+    int fw = 0;         // MMA warp: stages whose scores it has issued
+    int waited = 0;     // producer: stages whose copies it has waited for
+    int q_head = -1;    // MMA warp: the head whose queries are in the tile
+    int n_done = 0;     // stages processed
+    int cur_head = -1, cur_slot = -1, cur_vfirst = 0, cur_vlast = 0;
+    // MMA warp: the scores of stage j (its copies have landed), unless its
+    // record is the end record.
+    auto start_qk = [&](int j) {
+      fw = j + 1;
+      const int hj = meta[(j % depth) * 2].x;
+      if (hj < 0) return;
+      if (hj != q_head) {
+        q_head = hj;
+        load_q(hj);
+      }
+      issue_qk(j);
+    };
+    // The unit's two warps meet once more after the producer has written
+    // its first stage record, so that the MMA warp loads the first head's
+    // queries while the first copies are in flight (named barriers 5-8; the
+    // producer reaches it without waiting on anything).
+    auto pair_sync = [&]() {
+      switch (unit) {
+        case 0: named_barrier_sync<5>(64); break;
+        case 1: named_barrier_sync<6>(64); break;
+        case 2: named_barrier_sync<7>(64); break;
+        default: named_barrier_sync<8>(64); break;
+      }
+    };
+    if (!idle) {
+      if (producer) {
+        prepare_next();
+        for (int i = 0; i < depth; ++i) {
+          if (!issue(i)) {
+            send_end(i);
+            break;
+          }
+          ++issued;
+        }
+        pair_sync();
+      } else {
+        pair_sync();
+        const int h0 = meta[0].x;
+        if (h0 >= 0) {
+          q_head = h0;
+          load_q(h0);
+        }
+        if (wait_w(bars, 0u))
+          start_qk(0);
+        else
+          failed = true;
+      }
+      for (int it = 0; !failed; ++it) {
+        if (producer && it >= issued) break;
+        const int slot = it % depth;
+        // The stage's copies have landed; its record (or the end record,
+        // for the MMA warp) is visible.
+        if (!wait_w(bars + slot * 8, static_cast<uint32_t>((it / depth) & 1))) {
+          failed = true;
+          break;
+        }
+        if (producer) waited = it + 1;
+        const int4 m0 = meta[slot * 2];
+        const int4 m1 = meta[slot * 2 + 1];
+        if (m0.x < 0) break;  // end record (MMA warp)
+        const bool new_seg = m0.x != cur_head || m1.x != cur_slot;
+        bool o_done = it == 0;  // PV of the previous stage complete
+        if (new_seg) {
+          if (cur_head >= 0) {
+            if (!wait_w(ofree, static_cast<uint32_t>((it - 1) & 1))) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            o_done = true;
+            tc_finish(cur_head, cur_slot, cur_vfirst, cur_vlast);
+          }
+          cur_head = m0.x;
+          cur_slot = m1.x;
+          cur_vfirst = m1.z;
+          cur_vlast = m1.w;
+          m_run = -INFINITY;
+          l_run = 0.f;
+        }
+        if (!wait_w(sfull0 + (it & 1) * 8, static_cast<uint32_t>((it >> 1) & 1))) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[32];
+        tmem_ld32(t_lane + ucol + (it & 1) * 32, sr);
+        tmem_wait_ld();
+        // MMA warp: the next stage's scores now if its copies have landed
+        // (else after this stage's PV), so that they are ready when this
+        // stage is done.  The score buffer they overwrite was read by both
+        // warps before their arrivals for stage it - 1, which this warp
+        // waited for before that stage's PV.
+        if (!producer && fw < it + 2 &&
+            __all_sync(0xffffffffu, mbar_test_wait(bars + ((it + 1) % depth) * 8,
+                                                   static_cast<uint32_t>(((it + 1) / depth) & 1))))
+          start_qk(it + 1);
+        // Scores in log2 units; tokens past the stage's valid count masked.
+        const int ntok_stage = m0.z << log2_bs;
+        const int ntok_left = m0.w - (m0.y << log2_bs);
+        const int ntok = ntok_stage < ntok_left ? ntok_stage : ntok_left;
+        float sv[32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          sv[i] = half * 32 + i < ntok ? __uint_as_float(sr[i]) * scale_log2 : -INFINITY;
+          mx = fmaxf(mx, sv[i]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        // Lazy rescale: the running max moves only when a stage's max
+        // exceeds it by more than 8 (log2 units), so probabilities stay
+        // below 2^8 and the accumulator is rarely rescaled; the state (m,
+        // acc, l) is exact for any m.
+        const bool raise = mx > m_run + 8.f;  // always on a segment's first stage
+        const bool rescale = raise && m_run != -INFINITY;
+        const float m_new = raise ? mx : m_run;
+        const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
+        // Probabilities (type T), computed before the previous PV is waited for.
+        float ls = 0.f;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = fast_exp2(sv[2 * i] - m_new);
+          const float p1 = fast_exp2(sv[2 * i + 1] - m_new);
+          ls += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
+        }
+        l_run = l_run * alpha + ls;
+        m_run = m_new;
+        // The previous stage's PV is done: the probability tile and the
+        // accumulator may be written, and its slot refilled.
+        if (!o_done) {
+          if (!wait_w(ofree, static_cast<uint32_t>((it - 1) & 1))) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+          uint32_t o[64];
+          tmem_ld64(t_lane + ucol + 64, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 64; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st64(t_lane + ucol + 64, o);
+          tmem_wait_st();
+        }
+        // This unit's rows of the probability tile.
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = half * 4 + j;
+          st_shared_v4(ptile + row * 128 + static_cast<uint32_t>((c ^ (row & 7)) << 4), pk[4 * j],
+                       pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        }
+        // V rows past the valid tokens may hold stale or non-finite data:
+        // zero them so that 0 * V stays 0 (whole 128-byte rows).
+        if (ntok < ST) {
+          uint4* vz = reinterpret_cast<uint4*>(smem + (ring - smem_base) + slot * STAGE_BYTES + KV_BYTES);
+          for (int idx = role * 32 + lane; idx < (ST - ntok) * 8; idx += 64)
+            vz[(ntok + (idx >> 3)) * 8 + (idx & 7)] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();  // P and V writes, read by the tensor core
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pready);
+        n_done = it + 1;
+        if (producer) {
+          // The previous stage's slot is free (its PV is done).
+          if (it > 0 && !sent_end) {
+            const int fs = (it - 1) % depth;
+            if (issue(fs))
+              ++issued;
+            else
+              send_end(fs);
+          }
+        } else {
+          // Both warps' probability rows are in place: O (+)= P V.
+          if (!wait_w(pready, static_cast<uint32_t>(it & 1))) {
+            failed = true;
+            break;
+          }
+          issue_pv(it, !new_seg);
+          if (fw < it + 2) {
+            if (!wait_w(bars + ((it + 1) % depth) * 8, static_cast<uint32_t>(((it + 1) / depth) & 1))) {
+              failed = true;
+              break;
+            }
+            start_qk(it + 1);
+          }
+        }
+      }
+      // The last segment, after its last PV.
+      if (!failed && cur_head >= 0) {
+        if (wait_w(ofree, static_cast<uint32_t>((n_done - 1) & 1))) {
+          tc_fence_after();
+          tc_finish(cur_head, cur_slot, cur_vfirst, cur_vlast);
+        } else {
+          failed = true;
+        }
+      }
+      if (failed) {
+        ensure_waited();
+        if (lane == 0) atomicOr(p.status, kStatusTimeout);
+        // Copies in flight into this unit's ring (producer), then this
+        // warp's MMAs.
+        if (producer)
+          for (int j = waited; j < issued; ++j)
+            wait_w(bars + (j % depth) * 8, static_cast<uint32_t>((j / depth) & 1));
+        if (lane == 0) tc_commit(drain + role * 8);
+        __syncwarp();
+        wait_w(drain + role * 8, 0u);
+      }
+    }
+    ensure_waited();
+    // Every warp of the CTA arrives here; the allocating warp frees TMEM.
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+      tc_fence_after();
+      tmem_dealloc(tbase, tc_cols);
+    }
+  } else {
+  // ------------------------------------------------ mma.sync pipeline
   if (role == 0) {
     prepare_next();
     for (int i = 0; i < depth; ++i) {
@@ -1479,6 +1947,7 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64) ? 2 : 
   }
   if (cur_head >= 0) finish_head(cur_head, cur_slot, cur_vfirst, cur_vlast);
   ensure_waited();
+  }  // pipelines
 }
 
 

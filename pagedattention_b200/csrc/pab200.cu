@@ -127,22 +127,27 @@ struct LaunchCfg {
   }
 };
 
-template <typename T, int D, int NT, int ST, bool CORE, bool PAIR>
+template <typename T, int D, int NT, int ST, bool CORE, bool PAIR, bool TC>
 cudaError_t launch_decode(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
                           const CUtensorMap& k, const CUtensorMap& v,
                           const pab::DecodeParams& p) {
   LaunchCfg lc(grid, block, smem, s, pdl);
-  return cudaLaunchKernelEx(&lc.cfg, pab::decode_kernel<T, D, NT, ST, CORE, PAIR>, k, v, p);
+  return cudaLaunchKernelEx(&lc.cfg, pab::decode_kernel<T, D, NT, ST, CORE, PAIR, TC>, k, v, p);
 }
 
-template <typename T, int D, int NT, int ST, bool CORE = false, bool PAIR = false>
+template <typename T, int D, int NT, int ST, bool CORE = false, bool PAIR = false, bool TC = false>
 KernelOps ops_of() {
-  return KernelOps{reinterpret_cast<void*>(&pab::decode_kernel<T, D, NT, ST, CORE, PAIR>),
-                   &launch_decode<T, D, NT, ST, CORE, PAIR>};
+  return KernelOps{reinterpret_cast<void*>(&pab::decode_kernel<T, D, NT, ST, CORE, PAIR, TC>),
+                   &launch_decode<T, D, NT, ST, CORE, PAIR, TC>};
 }
 
 template <typename T, int ST>
-bool select_dnt(int D, int nt, bool core, bool pair, KernelOps* o) {
+bool select_dnt(int D, int nt, bool core, bool pair, bool tc, KernelOps* o) {
+  if (tc) {  // tcgen05 path: D 64, 64-token stages, two warps per ring
+    if (ST != 64 || D != 64 || !pair || nt != 2) return false;
+    *o = ops_of<T, 64, 2, 64, false, true, true>();
+    return true;
+  }
   if (pair) {  // two warps per ring, 16 query heads each
     if (nt != 2) return false;
     switch (D) {
@@ -170,19 +175,20 @@ bool select_dnt(int D, int nt, bool core, bool pair, KernelOps* o) {
   }
 }
 
-bool select_kernel(int dtype, int D, int nt, int st, bool core, bool pair, KernelOps* o) {
+bool select_kernel(int dtype, int D, int nt, int st, bool core, bool pair, bool tc,
+                   KernelOps* o) {
   if (dtype == PAB200_DTYPE_BF16) {
     switch (st) {
-      case 16: return select_dnt<__nv_bfloat16, 16>(D, nt, core, pair, o);
-      case 32: return select_dnt<__nv_bfloat16, 32>(D, nt, core, pair, o);
-      case 64: return select_dnt<__nv_bfloat16, 64>(D, nt, core, pair, o);
+      case 16: return !tc && select_dnt<__nv_bfloat16, 16>(D, nt, core, pair, false, o);
+      case 32: return !tc && select_dnt<__nv_bfloat16, 32>(D, nt, core, pair, false, o);
+      case 64: return select_dnt<__nv_bfloat16, 64>(D, nt, core, pair, tc, o);
       default: return false;
     }
   }
   switch (st) {
-    case 16: return select_dnt<__half, 16>(D, nt, core, pair, o);
-    case 32: return select_dnt<__half, 32>(D, nt, core, pair, o);
-    case 64: return select_dnt<__half, 64>(D, nt, core, pair, o);
+    case 16: return !tc && select_dnt<__half, 16>(D, nt, core, pair, false, o);
+    case 32: return !tc && select_dnt<__half, 32>(D, nt, core, pair, false, o);
+    case 64: return select_dnt<__half, 64>(D, nt, core, pair, tc, o);
     default: return false;
   }
 }
@@ -191,7 +197,7 @@ bool select_kernel(int dtype, int D, int nt, int st, bool core, bool pair, Kerne
 struct Plan {
   KernelOps ops;
   int G, nt, st, wpc, depth, ctas_per_sm, grid, W;
-  bool core, pair;
+  bool core, pair, tc;
   size_t smem;
   int n_heads;
   int slot_floats;
@@ -258,16 +264,24 @@ int validate(const pab200_decode_args* a, bool check_pointers) {
   return PAB200_OK;
 }
 
-// Dynamic shared memory of one decode CTA: ring slots, then per-warp
-// mbarriers, stage records and CUDA-core query scratch (see decode_kernel),
-// then the early-start page-count prefix (single-warp rings).  A paired
-// kernel has one ring (and a second set of mbarriers) per two warps.
-size_t decode_smem(int wpc, int depth, size_t stage, bool pair, int core_bytes) {
+// Dynamic shared memory of one decode CTA: ring slots, (tcgen05 path) the
+// query and probability tiles of every unit pair, then per-unit mbarriers,
+// stage records and CUDA-core query scratch (see decode_kernel), then the
+// early-start page-count prefix (single-warp rings).  A paired kernel has
+// one ring (and a second set of mbarriers) per two warps; the tcgen05 path
+// adds its own mbarriers and the tensor-memory address.
+size_t decode_smem(int wpc, int depth, size_t stage, bool pair, int core_bytes, bool tc) {
   const size_t units = pair ? size_t(wpc / 2) : size_t(wpc);
   return 1024 + units * depth * stage +
+         (tc ? (units + 1) / 2 * 2 * pab::kTcTileBytes : 0) +
          units * (pab::kMaxDepth * (8 + pab::kMetaBytesPerSlot) + core_bytes) +
-         (pair ? units * pab::kMaxDepth * 8 : size_t(pab::kEarlyBytes));
+         (pair ? units * pab::kMaxDepth * 8 : size_t(pab::kEarlyBytes)) +
+         (tc ? units * pab::kTcBarsPerUnit * 8 + 16 : 0);
 }
+
+// Tensor-memory columns one CTA of the tcgen05 path allocates (a power of
+// two; the kernel computes the same).
+int tc_cols(int units) { return units > 2 ? 512 : units * pab::kTcUnitCols; }
 
 struct Geometry {
   int wpc, per_sm;
@@ -280,7 +294,7 @@ struct Geometry {
 // memory and registers both limit it; ties go to the larger CTA).  Results
 // are cached per device, kernel, ring depth and stage size.
 int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, bool pair,
-                    int core_bytes, int forced_wpc, Geometry* out) {
+                    int core_bytes, bool tc, int forced_wpc, Geometry* out) {
   struct Entry {
     int dev;
     void* fn;
@@ -321,11 +335,14 @@ int choose_geometry(const KernelOps& ops, int dev, int depth, size_t stage, bool
   for (int ci = 0; ci < ncand; ++ci) {
     const int wpc = cand[ci];
     if (pair && (wpc & 1)) continue;  // warps come in pairs
-    const size_t smem = decode_smem(wpc, depth, stage, pair, core_bytes);
+    const size_t smem = decode_smem(wpc, depth, stage, pair, core_bytes, tc);
     if (smem > 232448) continue;
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops.fn, wpc * 32, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    // tcgen05 path: the resident CTAs' tensor memory must fit the SM's 512
+    // columns, so that no allocation waits for another CTA.
+    if (tc) per_sm = std::min(per_sm, 512 / tc_cols(wpc / 2));
     if (per_sm * wpc > best.per_sm * best.wpc) best = Geometry{wpc, per_sm, smem};
   }
   if (best.per_sm < 1) return fail(PAB200_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
@@ -357,9 +374,14 @@ int make_plan(const pab200_decode_args* a, Plan* pl, size_t scratch_cap,
   // pair), so pairs are used there only when PAB200_PAIR=1 asks for them.
   const bool pair_ok = pl->G > 16 && pl->G <= 32 && (D == 64 || D == 128);
   pl->pair = pair_ok && env_int("PAB200_PAIR", pl->G * D > 2048 ? 1 : 0) != 0;
+  // tcgen05 path (PAB200_TC=1): groups of 9-32 query heads at D = 64, on
+  // the 5th-generation tensor cores with TMEM accumulators; two warps per
+  // ring, 64-token stages.
+  pl->tc = pl->G > 8 && pl->G <= 32 && D == 64 && bs <= 64 && env_int("PAB200_TC", 0) != 0;
+  if (pl->tc) pl->pair = true;
   if (pl->pair) pl->nt = 2;
   // Tokens per ring stage: a power of two >= block_size.
-  pl->st = env_int("PAB200_ST", bs <= 32 ? 32 : 64);
+  pl->st = pl->tc ? 64 : env_int("PAB200_ST", bs <= 32 ? 32 : 64);
   if ((pl->st != 16 && pl->st != 32 && pl->st != 64) || pl->st < bs)
     return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_ST must be 16, 32 or 64 and >= block_size");
   const int nh = D / 64;
@@ -369,7 +391,8 @@ int make_plan(const pab200_decode_args* a, Plan* pl, size_t scratch_cap,
   // (PAB200_CORE=1) exists for query groups of at most 4 heads, 32-token
   // stages and D <= 128.
   pl->core = env_int("PAB200_CORE", 0) != 0 && pl->G <= pab::kCoreMaxG && pl->st == 32 && D <= 128;
-  if (!select_kernel(a->dtype, D, pl->nt, pl->st, pl->core, pl->pair, &pl->ops))
+  if (pl->tc) pl->core = false;
+  if (!select_kernel(a->dtype, D, pl->nt, pl->st, pl->core, pl->pair, pl->tc, &pl->ops))
     return fail(PAB200_ERR_UNSUPPORTED, "no kernel for head_size %d, group %d", D, pl->G);
 
   // Each warp owns a private ring of `depth` stages.  Throughput grows with
@@ -377,12 +400,15 @@ int make_plan(const pab200_decode_args* a, Plan* pl, size_t scratch_cap,
   // is a 2-deep ring and as many warps as ~200 KB of shared memory per SM
   // holds (6 warps at 16 KiB stages).
   const size_t stage = size_t(4) * pl->st * D;  // K + V bytes of one stage
-  int depth = env_int("PAB200_DEPTH", 2);
-  if (depth < 2 || depth > pab::kMaxDepth)
-    return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_DEPTH must be in [2, %d]", pab::kMaxDepth);
+  // The tcgen05 path computes the scores of the next stage while the warps
+  // work on the current one, so it needs a third stage in flight.
+  int depth = env_int("PAB200_DEPTH", pl->tc ? 3 : 2);
+  if (depth < (pl->tc ? 3 : 2) || depth > pab::kMaxDepth)
+    return fail(PAB200_ERR_INVALID_ARGUMENT, "PAB200_DEPTH must be in [%d, %d]", pl->tc ? 3 : 2,
+                pab::kMaxDepth);
   Geometry geo;
   if ((rc = choose_geometry(pl->ops, dev, depth, stage, pl->pair, pab::core_q_bytes(pl->core, D),
-                            env_int("PAB200_WPC", 0), &geo)))
+                            pl->tc, env_int("PAB200_WPC", 0), &geo)))
     return rc;
   const int wpc = geo.wpc, per_sm = geo.per_sm;
   pl->depth = depth;
