@@ -153,7 +153,8 @@ struct DecodeParams {
   int32_t steal_m_max;         // tail chunks per warp the workspace holds
   int32_t steal_pps;           // pages per ring stage (ST / block_size)
   int32_t steal_min_stages;    // smallest tail chunk, in ring stages
-  // Early start (no append, n_heads <= kEarlyMaxHeads, single-warp rings):
+  // Early start (no append, n_heads <= kEarlyMaxHeads, single-warp rings
+  // or the tcgen05 path):
   // the decode grid plans its own ranges and issues its first copies while
   // the planner runs; it waits for the planner only before touching shared
   // state (claims, outputs, status, empty heads).
@@ -699,10 +700,14 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64 && !TC)
   // stream write, as the host enables it only for calls without an append)
   // into shared memory — cum_sm [n_heads + 1], len_sm [n_heads] (clamped).
   // The planner computes the same prefix for the reduce kernel; both clamp
-  // alike, so ranges, tail chunks and segments agree.
-  const bool early = !PAIR && p.early != 0;
+  // alike, so ranges, tail chunks and segments agree.  The tcgen05 path
+  // keeps the prefix in its query / probability tiles, which it writes only
+  // after every warp of the CTA has switched to the planner's copy (early
+  // is cleared then).
+  bool early = (!PAIR || TC) && p.early != 0;
   int* const cum_sm = reinterpret_cast<int*>(
-      tail0 + upc * kMaxDepth * (8 + kMetaBytesPerSlot) + upc * core_q_bytes(CORE, D));
+      TC ? smem + upc * depth * STAGE_BYTES
+         : tail0 + upc * kMaxDepth * (8 + kMetaBytesPerSlot) + upc * core_q_bytes(CORE, D));
   int* const len_sm = cum_sm + kEarlyMaxHeads + 1;
   int W, total, first_head = 0, sm_m, sm_k;
   if (early) {
@@ -758,11 +763,13 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64 && !TC)
   // the CTA frees its tensor memory).
   const bool idle = gw >= W || total == 0 || gs >= g_end;
   if (idle) {
-    if (early) {
-      grid_dependency_wait();
-      zero_empty_heads();
+    if constexpr (!TC) {
+      if (early) {
+        grid_dependency_wait();
+        zero_empty_heads();
+      }
+      return;
     }
-    if constexpr (!TC) return;
   }
   // Current segment [c_gp, ge): the static prefix first, then tail chunks
   // claimed from the front of this warp's tail, then chunks stolen from the
@@ -1459,31 +1466,29 @@ __global__ void __launch_bounds__(kMaxWarpsPerCta * 32, (PAIR && D == 64 && !TC)
       }
       issue_qk(j);
     };
-    // The unit's two warps meet once more after the producer has written
-    // its first stage record, so that the MMA warp loads the first head's
-    // queries while the first copies are in flight (named barriers 5-8; the
-    // producer reaches it without waiting on anything).
-    auto pair_sync = [&]() {
-      switch (unit) {
-        case 0: named_barrier_sync<5>(64); break;
-        case 1: named_barrier_sync<6>(64); break;
-        case 2: named_barrier_sync<7>(64); break;
-        default: named_barrier_sync<8>(64); break;
-      }
-    };
-    if (!idle) {
-      if (producer) {
-        prepare_next();
-        for (int i = 0; i < depth; ++i) {
-          if (!issue(i)) {
-            send_end(i);
-            break;
-          }
-          ++issued;
+    // Prologue: the producers issue their first stages (on an early start,
+    // from the prefix in shared memory, before the planner has finished);
+    // then every warp waits for the plan and reads the prefix from global
+    // memory from here on, and a CTA barrier orders those reads before any
+    // tile write and publishes the first stage records, so that the MMA
+    // warps load the first head's queries while the first copies are in
+    // flight.  No warp waits on anything before the barrier except the
+    // plan.
+    if (!idle && producer) {
+      prepare_next();
+      for (int i = 0; i < depth; ++i) {
+        if (!issue(i)) {
+          send_end(i);
+          break;
         }
-        pair_sync();
-      } else {
-        pair_sync();
+        ++issued;
+      }
+    }
+    ensure_waited();
+    early = false;
+    __syncthreads();
+    if (!idle) {
+      if (!producer) {
         const int h0 = meta[0].x;
         if (h0 >= 0) {
           q_head = h0;

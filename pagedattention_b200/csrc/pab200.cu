@@ -670,8 +670,9 @@ int decode_impl(const pab200_decode_args* a, const Plan& pl, const pab::AppendPa
   p.append = app ? 1 : 0;
   // Early start of the decode grid (see DecodeParams::early): not with an
   // append (the planner writes the lengths and the cache the decode reads)
-  // nor with warp pairs, and only while the prefix fits shared memory.
-  p.early = !app && !pl.pair && pl.n_heads <= pab::kEarlyMaxHeads &&
+  // nor with mma.sync warp pairs, and only while the prefix fits shared
+  // memory (the tcgen05 path keeps it in its operand tiles).
+  p.early = !app && (!pl.pair || pl.tc) && pl.n_heads <= pab::kEarlyMaxHeads &&
             env_int("PAB200_EARLY", 1) != 0;
   if (app) {
     p.app = *app;

@@ -50,6 +50,22 @@ def test_random_vs_oracle(cuda_device, tc, G, bs, dtype):
     assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"tc G{G} bs{bs} {dtype}")
 
 
+@pytest.mark.parametrize("early", ["0", "1"])
+def test_with_and_without_early_start(cuda_device, tc, early):
+    """The decode grid plans its own ranges from the lengths before the
+    planner has finished (early start, the default at most 1024 heads), or
+    reads the planner's plan first; both give the same result."""
+    tc.setenv("PAB200_EARLY", early)
+    lens = _lens(4, 3, 8, 5)
+    q, k, v, sl, bt, scale = random_case(4, 3, 32, 64, 8, lens, torch.float16, seed=77,
+                                         k_scale=4.0)
+    dev = cuda_device
+    args = [t.to(dev) for t in (q, k, v, sl, bt)]
+    out = _decode(*args, scale)
+    assert_close(out, run_oracle(q, k, v, sl, bt, scale), what=f"early={early}")
+    assert torch.equal(out, _decode(*args, scale))
+
+
 def test_runs_the_tcgen05_kernel(cuda_device, tc):
     """The switch selects the tcgen05 kernel (no silent fallback)."""
     q, k, v, sl, bt, scale = random_case(2, 1, 32, 64, 8, [[700], [90]], torch.float16, seed=1)
