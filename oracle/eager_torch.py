@@ -1,6 +1,6 @@
 """CPU restatement of the reference's eager decode in PyTorch — TEST AND
-BASELINE INFRASTRUCTURE ONLY (imported by ``tests/`` and by ``bench.py``'s CPU
-baseline / reference arm; never by the product path).
+CPU-TIMING INFRASTRUCTURE ONLY (imported by ``tests/`` and by ``bench.py``'s
+CPU timing / reference arm; never by the product path).
 
 ``oracle/eager.py`` restates src/kernel_eager.py:6-56 in numpy with a thread
 pool over heads; it is the checker.  This module restates the same function
