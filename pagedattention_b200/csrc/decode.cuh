@@ -2313,9 +2313,10 @@ struct ExchangeParams {
   int32_t G;
 };
 
+// One block per row up to 1024 rows (a block's warps then split the row's
+// partial states between them), a few rows per block beyond.
 __host__ __device__ inline int64_t exchange_blocks(int64_t rows) {
-  const int64_t nb = (rows + 7) / 8;
-  return nb < 128 ? nb : 128;
+  return rows < 1 ? 1 : (rows < 1024 ? rows : 1024);
 }
 
 __device__ __forceinline__ uint64_t ll_word(float v, uint32_t e) {
@@ -2372,32 +2373,86 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const ExchangeParam
   grid_dependency_wait();
   if constexpr (DF > 0) {
     // 0. fused with the decode call: fold the split heads' partial states of
-    //    rows [r0, r1) into `state`, one warp per row, in slot order (the
-    //    reduce kernels' merge); rows of whole or empty heads were written
-    //    by the decode grid already.
+    //    rows [r0, r1) into `state` in slot order (the reduce kernels'
+    //    merge), one warp per row; rows of whole or empty heads were written
+    //    by the decode grid already.  With fewer rows than warps the warps
+    //    of a row split its partials into contiguous parts and the row's
+    //    first warp combines the parts in order (so the result depends
+    //    only on the segment count, not on timing).
     if (p.part) {
-      const int lane = tid & 31;
+      constexpr int NC = (DF + 127) / 128;
+      __shared__ float4 sacc[8][32][NC];
+      __shared__ float sml[8][2];
+      const int warp = tid >> 5, lane = tid & 31;
+      const int nw = blockDim.x >> 5;  // 8
+      const int rpb = static_cast<int>(r1 - r0);
+      int wpr = 1;  // warps per row
+      while (wpr < nw && wpr * 2 * rpb <= nw) wpr *= 2;
+      const int rows_per_round = nw / wpr;
+      const int sub = warp % wpr;
       const uint32_t hpar = *reinterpret_cast<const volatile uint32_t*>(p.parity) & 1u;
-      for (int64_t row = r0 + (tid >> 5); row < r1; row += blockDim.x / 32) {
-        const int hd = static_cast<int>(row / p.G), g = static_cast<int>(row - int64_t(hd) * p.G);
-        const int4 h4 = p.hseg[hd];
-        const int2 hs = hpar ? make_int2(h4.z, h4.w) : make_int2(h4.x, h4.y);
-        if (hs.y <= 1) continue;
-        const float* bs1[1] = {p.part + static_cast<int64_t>(hd + hs.x) * p.slot_floats};
-        const int g1[1] = {g}, a1[1] = {0}, b1[1] = {hs.y};
-        float M[1], L[1];
-        float4 acc[1][(DF + 127) / 128];
-        fold_rows<DF, 1, 16>(bs1, g1, a1, b1, p.slot_floats, p.G, lane, M, L, acc);
-        const float inv = 1.f / L[0];
-#pragma unroll
-        for (int i = 0; i < (DF + 127) / 128; ++i) {
-          const int c = lane * 4 + 128 * i;
-          if (c < DF)
-            *reinterpret_cast<float4*>(p.state + row * DF + c) =
-                make_float4(acc[0][i].x * inv, acc[0][i].y * inv, acc[0][i].z * inv,
-                            acc[0][i].w * inv);
+      for (int64_t base = r0; base < r1; base += rows_per_round) {
+        const int64_t row = base + warp / wpr;
+        int hd = 0, g = 0;
+        int2 hs = make_int2(0, 0);
+        if (row < r1) {
+          hd = static_cast<int>(row / p.G);
+          g = static_cast<int>(row - int64_t(hd) * p.G);
+          const int4 h4 = p.hseg[hd];
+          hs = hpar ? make_int2(h4.z, h4.w) : make_int2(h4.x, h4.y);
         }
-        if (lane == 0) p.state[rows * DF + row] = (M[0] + __log2f(L[0])) * kLn2;
+        const bool split = row < r1 && hs.y > 1;
+        float M[1] = {-INFINITY}, L[1] = {0.f};
+        float4 acc[1][NC];
+#pragma unroll
+        for (int i = 0; i < NC; ++i) acc[0][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (split) {
+          const float* bs1[1] = {p.part + static_cast<int64_t>(hd + hs.x) * p.slot_floats};
+          const int g1[1] = {g};
+          const int a1[1] = {sub * hs.y / wpr}, b1[1] = {(sub + 1) * hs.y / wpr};
+          fold_rows<DF, 1, 16>(bs1, g1, a1, b1, p.slot_floats, p.G, lane, M, L, acc);
+        }
+        if (wpr > 1) {
+          if (lane == 0) {
+            sml[warp][0] = M[0];
+            sml[warp][1] = L[0];
+          }
+#pragma unroll
+          for (int i = 0; i < NC; ++i) sacc[warp][lane][i] = acc[0][i];
+          __syncthreads();
+          if (split && sub == 0) {
+            for (int w = warp + 1; w < warp + wpr; ++w) {
+              const float mw = sml[w][0];
+              if (mw == -INFINITY) continue;  // an empty part
+              const float mn = fmaxf(M[0], mw);
+              const float sa = M[0] == -INFINITY ? 0.f : fast_exp2(M[0] - mn);
+              const float sb = fast_exp2(mw - mn);
+#pragma unroll
+              for (int i = 0; i < NC; ++i) {
+                const float4 v = sacc[w][lane][i];
+                acc[0][i].x = acc[0][i].x * sa + v.x * sb;
+                acc[0][i].y = acc[0][i].y * sa + v.y * sb;
+                acc[0][i].z = acc[0][i].z * sa + v.z * sb;
+                acc[0][i].w = acc[0][i].w * sa + v.w * sb;
+              }
+              L[0] = L[0] * sa + sml[w][1] * sb;
+              M[0] = mn;
+            }
+          }
+          __syncthreads();  // sacc / sml are reused by the next round
+        }
+        if (split && sub == 0) {
+          const float inv = 1.f / L[0];
+#pragma unroll
+          for (int i = 0; i < NC; ++i) {
+            const int c = lane * 4 + 128 * i;
+            if (c < DF)
+              *reinterpret_cast<float4*>(p.state + row * DF + c) =
+                  make_float4(acc[0][i].x * inv, acc[0][i].y * inv, acc[0][i].z * inv,
+                              acc[0][i].w * inv);
+          }
+          if (lane == 0) p.state[rows * DF + row] = (M[0] + __log2f(L[0])) * kLn2;
+        }
       }
       __syncthreads();  // the block's rows are final before they are sent
     }
